@@ -1,0 +1,191 @@
+/*
+ * llmik.h - C ABI of the B200 (sm_100a) GQA decode / KV-quantization library
+ * (libllmik_b200.so).
+ *
+ * Plain C: raw device pointers, 64-bit sizes, an opaque CUDA stream
+ * (cudaStream_t passed as void*; NULL = legacy default stream) and a status
+ * return. No torch types, no exceptions, no process abort: every entry point
+ * validates its arguments and returns a lik_status; lik_last_error() gives a
+ * human-readable detail for the calling thread's most recent failure.
+ *
+ * All launches are asynchronous on `stream`. Pointers must be device (or
+ * managed) memory of the current device. Tensor layouts are row-major and
+ * follow the reference extension (bindings/extension.cpp):
+ *
+ *   q, out          [batch, n_heads, head_dim]                     fp16
+ *   k, v (fp16)     [batch, n_kv_heads, kv_buf_len, head_dim]      fp16
+ *   k_q, v_q (int8) [batch, n_kv_heads, kv_buf_len, head_dim]      int8
+ *   k_q, v_q (int4) [batch, n_kv_heads, kv_buf_len, head_dim / 2]  packed,
+ *                   byte = (code[2i] & 0xF) | (code[2i+1] & 0xF) << 4
+ *   per-token scale / zero      [batch, n_kv_heads, kv_buf_len]               fp16
+ *   per-channel-group scale/zero [batch, n_kv_heads, n_groups_buf, head_dim]  fp16
+ *
+ * `seqlen` is the live KV length attended over (the first `seqlen` positions
+ * of each [kv_buf_len, ...] slab); kv_buf_len >= seqlen is the allocated
+ * length (row stride), as in bindings/extension.cpp:26-44. head_dim must be
+ * 128 and n_heads a multiple of n_kv_heads.
+ *
+ * Attention entry points use a caller-owned WORKSPACE (split-sequence partial
+ * results and per-unit completion counters). Size it with
+ * lik_decode_workspace_bytes() and zero it once with lik_workspace_init();
+ * every call leaves it zeroed again. Calls that may run concurrently (different
+ * streams) need different workspaces.
+ */
+#ifndef LLMIK_H
+#define LLMIK_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LLMIK_ABI_VERSION 1
+
+typedef enum lik_status {
+    LIK_OK = 0,
+    LIK_ERR_INVALID_ARGUMENT = 1,   /* null pointer, bad shape, seqlen > kv_buf_len, ... */
+    LIK_ERR_UNSUPPORTED = 2,        /* head_dim != 128 and similar */
+    LIK_ERR_MISALIGNED = 3,         /* a pointer lacks the 16-byte alignment required */
+    LIK_ERR_WORKSPACE = 4,          /* workspace missing or too small */
+    LIK_ERR_CUDA = 5,               /* a CUDA runtime call or launch failed */
+    LIK_ERR_DEVICE_TIMEOUT = 6      /* a bounded device-side wait gave up */
+} lik_status;
+
+/* ---- library information and errors ---------------------------------- */
+
+int lik_abi_version(void);
+const char* lik_status_string(lik_status status);
+/* Detail of the calling thread's last failing call ("" if none). */
+const char* lik_last_error(void);
+
+/* ---- workspace -------------------------------------------------------- */
+
+/* Upper bound of the workspace that the attention entry points need for this
+ * head configuration on the current device (independent of seqlen). */
+size_t lik_decode_workspace_bytes(int64_t batch, int64_t n_heads, int64_t n_kv_heads);
+
+/* Zero a workspace (cudaMemsetAsync on `stream`). Needed once after
+ * allocation. */
+lik_status lik_workspace_init(void* workspace, size_t workspace_bytes, void* stream);
+
+/* Read (and clear) the device error word that kernels set when a bounded
+ * device-side wait expires. Synchronizes `stream`. *device_error = 0 means no
+ * error. */
+lik_status lik_workspace_check(void* workspace, size_t workspace_bytes, void* stream,
+                               int* device_error);
+
+/* ---- decode attention (single query token per sequence) -------------- */
+
+/* fp16 KV. Replaces launch_decode_attention_splitk
+ * (kernels/attention/fused_attention_splitk.cu:233-250) and
+ * launch_decode_attention (kernels/attention/fused_attention.cu:110-119),
+ * declared in kernels/attention/fused_attention.cuh:17-41; op
+ * bindings/extension.cpp:26-83. */
+lik_status lik_decode_attention_f16(
+    const void* q, const void* k, const void* v, void* out,
+    int64_t batch, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim,
+    int64_t seqlen, int64_t kv_buf_len, float softmax_scale,
+    void* workspace, size_t workspace_bytes, void* stream);
+
+/* INT8 per-token KV: K = k_q * k_scale[token], V = v_q * v_scale[token].
+ * Replaces launch_decode_attention_int8
+ * (kernels/attention/fused_attention_int8.cu:109-122, declared
+ * fused_attention.cuh:54-60; op bindings/extension.cpp:152-194). Unlike the
+ * reference it also takes a live length / buffer stride. */
+lik_status lik_decode_attention_int8(
+    const void* q, const int8_t* k_q, const void* k_scale,
+    const int8_t* v_q, const void* v_scale, void* out,
+    int64_t batch, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim,
+    int64_t seqlen, int64_t kv_buf_len, float softmax_scale,
+    void* workspace, size_t workspace_bytes, void* stream);
+
+/* INT4 KIVI, symmetric (reference format): signed nibbles in [-7, 7];
+ * K = code * k_scale[group(token), channel], V = code * v_scale[token].
+ * Replaces launch_decode_attention_int4
+ * (kernels/attention/fused_attention_int4.cu:120-135, declared
+ * fused_attention.cuh:73-80; op bindings/extension.cpp:269-314).
+ * n_groups_buf is k_scale's group extent (k_scale.size(2) in the op);
+ * ceil(seqlen / group_size) <= n_groups_buf. */
+lik_status lik_decode_attention_int4(
+    const void* q, const int8_t* k_q, const void* k_scale,
+    const int8_t* v_q, const void* v_scale, void* out,
+    int64_t batch, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim,
+    int64_t seqlen, int64_t kv_buf_len, int64_t group_size, int64_t n_groups_buf,
+    float softmax_scale, void* workspace, size_t workspace_bytes, void* stream);
+
+/* INT4 KIVI, asymmetric (scale + zero; no reference counterpart, the format of
+ * the benchmark's INT4 configuration): unsigned nibbles 0..15;
+ * K = code * k_scale[g, c] + k_zero[g, c], V = code * v_scale[t] + v_zero[t]. */
+lik_status lik_decode_attention_int4_asym(
+    const void* q, const int8_t* k_q, const void* k_scale, const void* k_zero,
+    const int8_t* v_q, const void* v_scale, const void* v_zero, void* out,
+    int64_t batch, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim,
+    int64_t seqlen, int64_t kv_buf_len, int64_t group_size, int64_t n_groups_buf,
+    float softmax_scale, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- KV quantize / pack --------------------------------------------- */
+/*
+ * Source x: [batch, n_kv_heads, n_tokens, head_dim] fp16, contiguous.
+ * Destination: a cache of allocated length dst_buf_len (>= dst_pos + n_tokens);
+ * the n_tokens quantized rows land at positions [dst_pos, dst_pos + n_tokens)
+ * of every (batch, kv_head) slab. With dst_pos = 0 and dst_buf_len = n_tokens
+ * this is the reference op's contiguous output.
+ *
+ * Codes are bit-identical to reference/kv_cache_ref.py on x.float():
+ * scale = max(absmax / qmax, 1e-8) and code = clamp(rint(x / scale)) with IEEE
+ * division and round-half-to-even; the stored scale is fp16(scale).
+ */
+
+/* INT8 per token. Replaces launch_quantize_per_token
+ * (kernels/kv_cache/kv_compress.cu:69-79, decl kv_compress.cuh:19-22; op
+ * bindings/extension.cpp:120-146). */
+lik_status lik_quantize_per_token_int8(
+    const void* x, int8_t* codes, void* scale,
+    int64_t batch, int64_t n_kv_heads, int64_t n_tokens, int64_t head_dim,
+    int64_t dst_pos, int64_t dst_buf_len, void* stream);
+
+/* INT4 per token, packed (KIVI V). Replaces launch_quantize_v_per_token_int4
+ * (kernels/kv_cache/kv_compress.cu:219-228, decl kv_compress.cuh:44-48; op
+ * bindings/extension.cpp:235-261). */
+lik_status lik_quantize_v_per_token_int4(
+    const void* x, int8_t* packed, void* scale,
+    int64_t batch, int64_t n_kv_heads, int64_t n_tokens, int64_t head_dim,
+    int64_t dst_pos, int64_t dst_buf_len, void* stream);
+
+/* INT4 per channel over groups of group_size tokens, packed (KIVI K). The
+ * short last group uses its real tokens (the reference zero-pads, which leaves
+ * an absolute maximum unchanged). dst_pos must be a multiple of group_size;
+ * scales land at groups [dst_pos / group_size, ...) of a scale buffer with
+ * n_groups_buf groups. Replaces launch_quantize_k_per_channel_groupwise_int4
+ * (kernels/kv_cache/kv_compress.cu:159-170, decl kv_compress.cuh:36-40; op
+ * bindings/extension.cpp:200-229). */
+lik_status lik_quantize_k_per_channel_groupwise_int4(
+    const void* x, int8_t* packed, void* scale,
+    int64_t batch, int64_t n_kv_heads, int64_t n_tokens, int64_t head_dim,
+    int64_t group_size, int64_t dst_pos, int64_t dst_buf_len, int64_t n_groups_buf,
+    void* stream);
+
+/* Asymmetric INT4 per token (V side of the asymmetric KIVI format; no
+ * reference counterpart): scale = fp16(max((max - min) / 15, 2^-24)),
+ * zero = fp16(min), code = clamp(rint((x - zero) / scale), 0, 15) using the
+ * stored fp16 scale and zero. */
+lik_status lik_quantize_v_per_token_int4_asym(
+    const void* x, int8_t* packed, void* scale, void* zero,
+    int64_t batch, int64_t n_kv_heads, int64_t n_tokens, int64_t head_dim,
+    int64_t dst_pos, int64_t dst_buf_len, void* stream);
+
+/* Asymmetric INT4 per channel over token groups (K side; no reference
+ * counterpart). Same group rules as the symmetric K entry point. */
+lik_status lik_quantize_k_per_channel_groupwise_int4_asym(
+    const void* x, int8_t* packed, void* scale, void* zero,
+    int64_t batch, int64_t n_kv_heads, int64_t n_tokens, int64_t head_dim,
+    int64_t group_size, int64_t dst_pos, int64_t dst_buf_len, int64_t n_groups_buf,
+    void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* LLMIK_H */

@@ -1,0 +1,860 @@
+// Single-query GQA decode attention over an fp16 / INT8-per-token / INT4-KIVI
+// KV cache for sm_100a, with the dequantization fused into a split-sequence
+// (FlashDecoding) loop and the log-sum-exp combine fused into the same launch.
+//
+// Work decomposition
+//   unit  = (batch, kv_head, head block): HB query heads that share one KV
+//           slab (HB = the GQA group, or a divisor of it), so every KV byte is
+//           read from HBM exactly once per step (the reference launches one
+//           CTA per query head and re-reads each slab G times, relying on L2).
+//   tile  = T consecutive KV positions of one unit (T * row bytes = 32 KB).
+//   The flattened (unit, tile) sequence is split evenly over a persistent grid
+//   of one CTA per SM: CTA c owns tiles [c*TT/C, (c+1)*TT/C). A CTA's range may
+//   cover whole units (written straight to `out`) and partial units at its
+//   two ends (written as an un-normalised partial to the workspace; the CTA
+//   that completes a unit's last partial, found with an atomic ticket, merges
+//   them). No CTA ever waits for another CTA.
+//
+// Inside a CTA
+//   warp 8 (producer): one lane issues 1-D bulk async copies
+//     (cp.async.bulk, no tensor map, no multicast) of the K and V tile plus the
+//     per-token / per-group scales into an NST-deep shared-memory ring, each
+//     stage tracked by a "full" mbarrier with transaction bytes and an "empty"
+//     mbarrier the consumers arrive on.
+//   warps 0-7 (consumers): warp w owns positions [w*T/8, (w+1)*T/8) of every
+//     tile and keeps its own online-softmax state (m, l, acc) for all HB heads,
+//     so the tile loop has no CTA-wide barrier. Per warp and tile:
+//       QK : 8 lanes per position, 16 channels per lane, packed half2 FMAs on
+//            dequantized codes (the K group scale of INT4 is folded into q once
+//            per group, the INT8 token scale applied to the reduced score),
+//            partial sums reduce-scattered over the 8 lanes so each lane ends
+//            with one head's score.
+//       softmax: scores are in the log2 domain (q pre-scaled by
+//            softmax_scale * log2 e); warp-shuffle max/sum; exp2 on MUFU.
+//       PV : lanes own output channels, fp32 accumulation; the V token scale is
+//            folded into p, the asymmetric V zero point into a per-head sum.
+//   At a unit boundary the 8 warp states are merged in shared memory.
+//
+// Every mbarrier wait is bounded (kMaxPolls); on expiry the kernel records
+// kDevWaitTimeout in the workspace error word, stops issuing copies, drains
+// the copies it has in flight (again bounded) and returns.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <mutex>
+
+#include "lik_device.cuh"
+#include "lik_internal.h"
+
+namespace lik {
+
+constexpr int kNCW = 8;                    // consumer warps
+constexpr int kThreads = (kNCW + 1) * 32;  // + producer warp
+constexpr float kLog2e = 1.4426950408889634f;
+
+template <int FMT>
+struct Fmt;
+template <>
+struct Fmt<kF16> {
+    static constexpr int ROWB = 256, T = 64, PVC = 4;
+    static constexpr bool TOKK = false, TOKV = false, ZV = false, KG = false, ZK = false, SIGNED = true;
+};
+template <>
+struct Fmt<kI8> {
+    static constexpr int ROWB = 128, T = 128, PVC = 4;
+    static constexpr bool TOKK = true, TOKV = true, ZV = false, KG = false, ZK = false, SIGNED = true;
+};
+template <>
+struct Fmt<kI4Sym> {
+    static constexpr int ROWB = 64, T = 256, PVC = 8;
+    static constexpr bool TOKK = false, TOKV = true, ZV = false, KG = true, ZK = false, SIGNED = true;
+};
+template <>
+struct Fmt<kI4Asym> {
+    static constexpr int ROWB = 64, T = 256, PVC = 8;
+    static constexpr bool TOKK = false, TOKV = true, ZV = true, KG = true, ZK = true, SIGNED = false;
+};
+
+struct DecodeParams {
+    const __half* q;
+    __half* out;
+    const uint8_t* k;
+    const uint8_t* v;
+    const __half* ks;
+    const __half* vs;
+    const __half* kz;
+    const __half* vz;
+    long long seqlen, kv_buf_len, ng_buf;
+    long long n_units, tpu, total_tiles;
+    int n_heads, n_kv_heads, nhb;
+    int group_size, tok_bulk, kg_smem, ngt;
+    int n_ctas, nst, stage_bytes;
+    int off_v, off_ks, off_vs, off_vz, off_kgs, off_kgz;
+    int off_work, off_ml, off_misc, off_bar;
+    float qscale;
+    float* part;
+    unsigned* counters;
+    int* err;
+};
+
+// ---- small helpers --------------------------------------------------------
+
+template <int HB>
+__device__ __forceinline__ int head_of_lane(int lane) {
+    int h = 0;
+#pragma unroll
+    for (int L = 0, n = HB; L < 3 && n > 1; ++L, n >>= 1) h += ((lane >> L) & 1) * (n >> 1);
+    return h;
+}
+
+template <int HB>
+__device__ __forceinline__ int lane_of_head(int h) {
+    int lane = 0;
+#pragma unroll
+    for (int L = 0, n = HB; L < 3 && n > 1; ++L, n >>= 1) lane |= ((h / (n >> 1)) & 1) << L, h %= (n >> 1);
+    return lane;
+}
+
+// True for the one lane per (8-lane group, head) whose non-split lane bits are 0.
+template <int HB>
+__device__ __forceinline__ bool head_primary(int lane) {
+    constexpr int used = HB >= 8 ? 3 : HB >= 4 ? 2 : HB >= 2 ? 1 : 0;
+    return ((lane & 7) >> used) == 0;
+}
+
+// Sum v[0..HB) over the 8 lanes of a group (lane bits 0..2), scattering heads:
+// afterwards the lane holds the full sum of head head_of_lane<HB>(lane).
+template <int HB>
+__device__ __forceinline__ float reduce_scatter8(float (&v)[HB], int lane) {
+    float a[HB];
+#pragma unroll
+    for (int i = 0; i < HB; ++i) a[i] = v[i];
+    int n = HB;
+#pragma unroll
+    for (int L = 0; L < 3; ++L) {
+        const int m = 1 << L;
+        if (n > 1) {
+            const int half = n >> 1;
+            const bool up = (lane >> L) & 1;
+#pragma unroll
+            for (int i = 0; i < HB / 2; ++i) {
+                if (i < half) {
+                    const float send = up ? a[i] : a[i + half];
+                    const float keep = up ? a[i + half] : a[i];
+                    a[i] = keep + __shfl_xor_sync(kFull, send, m);
+                }
+            }
+            n = half;
+        } else {
+            a[0] += __shfl_xor_sync(kFull, a[0], m);
+        }
+    }
+    return a[0];
+}
+
+__device__ __forceinline__ long long owner_cta(long long tile, long long total, int nctas) {
+    return ((tile + 1) * nctas - 1) / total;
+}
+__device__ __forceinline__ long long cta_first_tile(long long c, long long total, int nctas) {
+    return c * total / nctas;
+}
+
+__device__ __forceinline__ float h2_sum(half2 a) {
+    const float2 f = __half22float2(a);
+    return f.x + f.y;
+}
+
+// ---- the kernel -----------------------------------------------------------
+
+template <int FMT, int HB>
+__global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams p) {
+    using F = Fmt<FMT>;
+    constexpr int T = F::T;
+    constexpr int ROWB = F::ROWB;
+    constexpr int TW = T / kNCW;  // positions per warp per tile
+    constexpr int NP = TW / 4;    // QK passes (4 positions per pass)
+    constexpr int PVC = F::PVC;
+    constexpr int SL = HB * kHeadDim + 2 * HB;  // partial slot stride (floats)
+
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_bar);
+    uint64_t* empty = full + p.nst;
+    volatile int* misc = reinterpret_cast<volatile int*>(smem + p.off_misc);
+
+    const long long cta = blockIdx.x;
+    const long long tb = cta_first_tile(cta, p.total_tiles, p.n_ctas);
+    const long long te = cta_first_tile(cta + 1, p.total_tiles, p.n_ctas);
+
+    if (tid == 0) {
+        for (int s = 0; s < p.nst; ++s) {
+            mbar_init(&full[s], 32);
+            mbar_init(&empty[s], kNCW);
+        }
+        misc[0] = 0;
+        misc[1] = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    // ======================= producer warp ================================
+    if (warp == kNCW) {
+        const uint64_t pol = l2_policy_evict_first();
+        long long j = 0;
+        bool ok = true;
+        for (long long i = tb; i < te; ++i, ++j) {
+            const int st = static_cast<int>(j % p.nst);
+            if (j >= p.nst) {
+                const uint32_t par = static_cast<uint32_t>(((j / p.nst) - 1) & 1);
+                bool got = false;
+                for (uint32_t it = 0; it < kMaxPolls; ++it) {
+                    if (mbar_try_wait(&empty[st], par)) {
+                        got = true;
+                        break;
+                    }
+                    if (misc[0]) break;
+                }
+                if (!got) {
+                    ok = false;
+                    break;
+                }
+            }
+            const long long unit = i / p.tpu;
+            const long long ti = i - unit * p.tpu;
+            const long long t0 = ti * T;
+            const int ntok = static_cast<int>(min(static_cast<long long>(T), p.seqlen - t0));
+            const long long bk = unit / p.nhb;
+            const long long rowbase = bk * p.kv_buf_len + t0;
+            uint8_t* sb = smem + static_cast<size_t>(st) * p.stage_bytes;
+            const int n8 = (ntok + 7) & ~7;
+
+            // Scales that cannot use a bulk copy (unaligned slabs): plain loads.
+            if ((F::TOKK || F::TOKV) && !p.tok_bulk) {
+                for (int t = lane; t < ntok; t += 32) {
+                    if (F::TOKK) reinterpret_cast<__half*>(sb + p.off_ks)[t] = p.ks[rowbase + t];
+                    if (F::TOKV) reinterpret_cast<__half*>(sb + p.off_vs)[t] = p.vs[rowbase + t];
+                    if (F::ZV) reinterpret_cast<__half*>(sb + p.off_vz)[t] = p.vz[rowbase + t];
+                }
+            }
+            if (lane == 0) {
+                uint32_t bytes = 2u * ntok * ROWB;
+                int g0 = 0, ngrp = 0;
+                if ((F::TOKK || F::TOKV) && p.tok_bulk) {
+                    bytes += (F::TOKK + F::TOKV + F::ZV) * n8 * 2;
+                }
+                if (F::KG && p.kg_smem) {
+                    g0 = static_cast<int>(t0 / p.group_size);
+                    const int g1 = static_cast<int>((t0 + ntok - 1) / p.group_size);
+                    ngrp = g1 - g0 + 1;
+                    bytes += (F::ZK ? 2 : 1) * ngrp * kHeadDim * 2;
+                }
+                mbar_arrive_expect_tx(&full[st], bytes);
+                bulk_g2s(sb, p.k + rowbase * ROWB, ntok * ROWB, &full[st], pol);
+                bulk_g2s(sb + p.off_v, p.v + rowbase * ROWB, ntok * ROWB, &full[st], pol);
+                if ((F::TOKK || F::TOKV) && p.tok_bulk) {
+                    if (F::TOKK) bulk_g2s(sb + p.off_ks, p.ks + rowbase, n8 * 2, &full[st], pol);
+                    if (F::TOKV) bulk_g2s(sb + p.off_vs, p.vs + rowbase, n8 * 2, &full[st], pol);
+                    if (F::ZV) bulk_g2s(sb + p.off_vz, p.vz + rowbase, n8 * 2, &full[st], pol);
+                }
+                if (F::KG && p.kg_smem) {
+                    const long long gb = (bk * p.ng_buf + g0) * kHeadDim;
+                    bulk_g2s(sb + p.off_kgs, p.ks + gb, ngrp * kHeadDim * 2, &full[st], pol);
+                    if (F::ZK) bulk_g2s(sb + p.off_kgz, p.kz + gb, ngrp * kHeadDim * 2, &full[st], pol);
+                }
+            } else {
+                mbar_arrive(&full[st]);
+            }
+        }
+        if (!ok) {
+            // Let the copies already issued land before the CTA can exit.
+            const long long first = j > p.nst ? j - p.nst : 0;
+            for (long long jj = first; jj < j; ++jj) {
+                mbar_wait_bounded(&full[jj % p.nst], static_cast<uint32_t>((jj / p.nst) & 1));
+            }
+            if (lane == 0) atomicExch(p.err, kDevWaitTimeout);
+        }
+        return;
+    }
+
+    // ======================= consumer warps ===============================
+    const int w = warp;
+    const int grp = lane >> 3;
+    const int jl = lane & 7;
+    const int hh = head_of_lane<HB>(lane);
+    const bool prim = head_primary<HB>(lane);
+    const int nct = kNCW * 32;
+
+    float* pbuf = reinterpret_cast<float*>(smem + p.off_work) + w * TW * HB;
+    float* abuf = reinterpret_cast<float*>(smem + p.off_work);
+    float* mlb = reinterpret_cast<float*>(smem + p.off_ml);
+
+    float m_run = -INFINITY, l_run = 0.f, z_run = 0.f;
+    float acc[HB][PVC];
+    uint32_t qh[HB][8];  // q * softmax_scale * log2e as half2, in the format's pair order
+    uint32_t qs[HB][8];  // INT4: qh * k group scale
+    float qb[HB];        // INT4 asym: sum over the lane's channels of qh * k group zero
+    long long cur_unit = -1, seg_t0 = 0, qoff = 0, bk = 0;
+    int cur_g = -1;
+    bool aborted = false;
+
+#pragma unroll
+    for (int h = 0; h < HB; ++h) {
+        qb[h] = 0.f;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) qs[h][c] = 0u;
+    }
+
+    long long j = 0;
+    for (long long i = tb; i < te; ++i, ++j) {
+        const long long unit = i / p.tpu;
+        const long long ti = i - unit * p.tpu;
+        if (unit != cur_unit) {
+            // ---- start of a unit segment: load q for the HB heads ----
+            cur_unit = unit;
+            seg_t0 = ti;
+            cur_g = -1;
+            bk = unit / p.nhb;
+            const int hb = static_cast<int>(unit - bk * p.nhb);
+            const long long b = bk / p.n_kv_heads;
+            const int kvh = static_cast<int>(bk - b * p.n_kv_heads);
+            qoff = (b * p.n_heads + static_cast<long long>(kvh) * p.nhb * HB + hb * HB) * kHeadDim;
+            m_run = -INFINITY;
+            l_run = 0.f;
+            z_run = 0.f;
+#pragma unroll
+            for (int h = 0; h < HB; ++h) {
+#pragma unroll
+                for (int c = 0; c < PVC; ++c) acc[h][c] = 0.f;
+                const __half* qp = p.q + qoff + h * kHeadDim;
+                // the lane's 16 QK channels, as 16 halves in channel order
+                uint4 ua, ub;
+                if (FMT == kF16) {
+                    ua = *reinterpret_cast<const uint4*>(qp + 8 * jl);
+                    ub = *reinterpret_cast<const uint4*>(qp + 64 + 8 * jl);
+                } else {
+                    ua = *reinterpret_cast<const uint4*>(qp + 16 * jl);
+                    ub = *reinterpret_cast<const uint4*>(qp + 16 * jl + 8);
+                }
+                const __half* ha = reinterpret_cast<const __half*>(&ua);
+                const __half* hbv = reinterpret_cast<const __half*>(&ub);
+                float qf[16];
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    qf[c] = __half2float(ha[c]) * p.qscale;
+                    qf[8 + c] = __half2float(hbv[c]) * p.qscale;
+                }
+                if (F::KG) {
+                    // pair (wd*4 + k) = channels (8wd + k, 8wd + k + 4) of the lane's 16
+#pragma unroll
+                    for (int wd = 0; wd < 2; ++wd)
+#pragma unroll
+                        for (int k = 0; k < 4; ++k)
+                            qh[h][wd * 4 + k] = as_u32(__floats2half2_rn(qf[8 * wd + k], qf[8 * wd + k + 4]));
+                } else {
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) qh[h][c] = as_u32(__floats2half2_rn(qf[2 * c], qf[2 * c + 1]));
+                }
+            }
+        }
+
+        const int st = static_cast<int>(j % p.nst);
+        if (!aborted) {
+            if (misc[0] || !mbar_wait_bounded(&full[st], static_cast<uint32_t>((j / p.nst) & 1))) {
+                aborted = true;
+                misc[0] = 1;
+                if (lane == 0) atomicExch(p.err, kDevWaitTimeout);
+            }
+        }
+
+        const long long t0 = ti * T;
+        const int ntok = static_cast<int>(min(static_cast<long long>(T), p.seqlen - t0));
+        const uint8_t* sb = smem + static_cast<size_t>(st) * p.stage_bytes;
+        const int wt0 = w * TW;
+
+        if (!aborted && wt0 < ntok) {
+            const uint8_t* sK = sb;
+            const uint8_t* sV = sb + p.off_v;
+            const __half* sks = reinterpret_cast<const __half*>(sb + p.off_ks);
+            const __half* svs = reinterpret_cast<const __half*>(sb + p.off_vs);
+            const __half* svz = reinterpret_cast<const __half*>(sb + p.off_vz);
+            const int nval = min(TW, ntok - wt0);
+
+            // ---------------- QK ----------------
+            float sc[NP];
+#pragma unroll
+            for (int pp = 0; pp < NP; ++pp) {
+                const int tt = wt0 + pp * 4 + grp;
+                float part[HB];
+                if (tt < ntok) {
+                    const uint8_t* row = sK + tt * ROWB;
+                    if (FMT == kF16) {
+                        const uint4 ka = *reinterpret_cast<const uint4*>(row + jl * 16);
+                        const uint4 kb = *reinterpret_cast<const uint4*>(row + 128 + jl * 16);
+                        const uint32_t kk[8] = {ka.x, ka.y, ka.z, ka.w, kb.x, kb.y, kb.z, kb.w};
+#pragma unroll
+                        for (int h = 0; h < HB; ++h) {
+                            half2 a = __hmul2(as_h2(qh[h][0]), as_h2(kk[0]));
+#pragma unroll
+                            for (int c = 1; c < 8; ++c) a = __hfma2(as_h2(qh[h][c]), as_h2(kk[c]), a);
+                            part[h] = h2_sum(a);
+                        }
+                    } else if (FMT == kI8) {
+                        const uint4 ka = *reinterpret_cast<const uint4*>(row + jl * 16);
+                        half2 kk[8];
+                        i8x4_to_h2(ka.x, kk[0], kk[1]);
+                        i8x4_to_h2(ka.y, kk[2], kk[3]);
+                        i8x4_to_h2(ka.z, kk[4], kk[5]);
+                        i8x4_to_h2(ka.w, kk[6], kk[7]);
+#pragma unroll
+                        for (int h = 0; h < HB; ++h) {
+                            half2 a = __hmul2(as_h2(qh[h][0]), kk[0]);
+#pragma unroll
+                            for (int c = 1; c < 8; ++c) a = __hfma2(as_h2(qh[h][c]), kk[c], a);
+                            part[h] = h2_sum(a);
+                        }
+                    } else {
+                        // INT4: fold the K group scale (and zero) into q on group change
+                        const int g = static_cast<int>((t0 + tt) / p.group_size);
+                        if (g != cur_g) {
+                            cur_g = g;
+                            const __half* gs;
+                            const __half* gz = nullptr;
+                            if (p.kg_smem) {
+                                const int g0 = static_cast<int>(t0 / p.group_size);
+                                gs = reinterpret_cast<const __half*>(sb + p.off_kgs) + (g - g0) * kHeadDim;
+                                if (F::ZK) gz = reinterpret_cast<const __half*>(sb + p.off_kgz) + (g - g0) * kHeadDim;
+                            } else {
+                                const long long gb = (bk * p.ng_buf + g) * kHeadDim;
+                                gs = p.ks + gb;
+                                if (F::ZK) gz = p.kz + gb;
+                            }
+                            const uint4 s0 = *reinterpret_cast<const uint4*>(gs + 16 * jl);
+                            const uint4 s1 = *reinterpret_cast<const uint4*>(gs + 16 * jl + 8);
+                            const __half* sh0 = reinterpret_cast<const __half*>(&s0);
+                            const __half* sh1 = reinterpret_cast<const __half*>(&s1);
+                            half2 sp[8];
+#pragma unroll
+                            for (int k = 0; k < 4; ++k) {
+                                sp[k] = __halves2half2(sh0[k], sh0[k + 4]);
+                                sp[4 + k] = __halves2half2(sh1[k], sh1[k + 4]);
+                            }
+#pragma unroll
+                            for (int h = 0; h < HB; ++h)
+#pragma unroll
+                                for (int c = 0; c < 8; ++c) qs[h][c] = as_u32(__hmul2(as_h2(qh[h][c]), sp[c]));
+                            if (F::ZK) {
+                                const uint4 z0 = *reinterpret_cast<const uint4*>(gz + 16 * jl);
+                                const uint4 z1 = *reinterpret_cast<const uint4*>(gz + 16 * jl + 8);
+                                const __half* zh0 = reinterpret_cast<const __half*>(&z0);
+                                const __half* zh1 = reinterpret_cast<const __half*>(&z1);
+                                half2 zp[8];
+#pragma unroll
+                                for (int k = 0; k < 4; ++k) {
+                                    zp[k] = __halves2half2(zh0[k], zh0[k + 4]);
+                                    zp[4 + k] = __halves2half2(zh1[k], zh1[k + 4]);
+                                }
+#pragma unroll
+                                for (int h = 0; h < HB; ++h) {
+                                    float s = 0.f;
+#pragma unroll
+                                    for (int c = 0; c < 8; ++c) {
+                                        const float2 a = __half22float2(as_h2(qh[h][c]));
+                                        const float2 z = __half22float2(zp[c]);
+                                        s = fmaf(a.x, z.x, fmaf(a.y, z.y, s));
+                                    }
+                                    qb[h] = s;
+                                }
+                            }
+                        }
+                        const uint2 kw = *reinterpret_cast<const uint2*>(row + jl * 8);
+                        half2 c0[4], c1[4];
+                        i4x8_to_h2<F::SIGNED>(kw.x, c0);
+                        i4x8_to_h2<F::SIGNED>(kw.y, c1);
+#pragma unroll
+                        for (int h = 0; h < HB; ++h) {
+                            half2 a = __hmul2(as_h2(qs[h][0]), c0[0]);
+#pragma unroll
+                            for (int c = 1; c < 4; ++c) a = __hfma2(as_h2(qs[h][c]), c0[c], a);
+#pragma unroll
+                            for (int c = 0; c < 4; ++c) a = __hfma2(as_h2(qs[h][4 + c]), c1[c], a);
+                            part[h] = h2_sum(a) + (F::ZK ? qb[h] : 0.f);
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int h = 0; h < HB; ++h) part[h] = 0.f;
+                }
+                float s = reduce_scatter8<HB>(part, lane);
+                if (tt >= ntok) {
+                    s = -INFINITY;
+                } else if (F::TOKK) {
+                    s *= __half2float(sks[tt]);
+                }
+                sc[pp] = s;
+            }
+
+            // ---------------- online softmax (log2 domain) ----------------
+            float mloc = sc[0];
+#pragma unroll
+            for (int pp = 1; pp < NP; ++pp) mloc = fmaxf(mloc, sc[pp]);
+            mloc = fmaxf(mloc, __shfl_xor_sync(kFull, mloc, 8));
+            mloc = fmaxf(mloc, __shfl_xor_sync(kFull, mloc, 16));
+            const float mnew = fmaxf(m_run, mloc);
+            const float alpha = fast_exp2(m_run - mnew);
+            float ls = 0.f, zs = 0.f;
+#pragma unroll
+            for (int pp = 0; pp < NP; ++pp) {
+                const int tl = pp * 4 + grp;  // position within the warp's share
+                const float e = fast_exp2(sc[pp] - mnew);
+                ls += e;
+                if (tl < nval) {
+                    float pv = e;
+                    if (F::TOKV) pv *= __half2float(svs[wt0 + tl]);
+                    if (F::ZV) zs = fmaf(e, __half2float(svz[wt0 + tl]), zs);
+                    if (prim) pbuf[tl * HB + hh] = pv;
+                }
+            }
+            ls += __shfl_xor_sync(kFull, ls, 8);
+            ls += __shfl_xor_sync(kFull, ls, 16);
+            if (F::ZV) {
+                zs += __shfl_xor_sync(kFull, zs, 8);
+                zs += __shfl_xor_sync(kFull, zs, 16);
+            }
+            l_run = fmaf(l_run, alpha, ls);
+            z_run = fmaf(z_run, alpha, zs);
+            m_run = mnew;
+            float al[HB];
+#pragma unroll
+            for (int h = 0; h < HB; ++h) al[h] = __shfl_sync(kFull, alpha, lane_of_head<HB>(h));
+            __syncwarp();
+#pragma unroll
+            for (int h = 0; h < HB; ++h)
+#pragma unroll
+                for (int c = 0; c < PVC; ++c) acc[h][c] *= al[h];
+
+            // ---------------- PV ----------------
+            if (FMT == kF16 || FMT == kI8) {
+                for (int t = 0; t < nval; ++t) {
+                    float vf[4];
+                    if (FMT == kF16) {
+                        const uint2 vv = *reinterpret_cast<const uint2*>(sV + (wt0 + t) * ROWB + lane * 8);
+                        const float2 a = __half22float2(as_h2(vv.x));
+                        const float2 b = __half22float2(as_h2(vv.y));
+                        vf[0] = a.x; vf[1] = a.y; vf[2] = b.x; vf[3] = b.y;
+                    } else {
+                        const uint32_t vv = *reinterpret_cast<const uint32_t*>(sV + (wt0 + t) * ROWB + lane * 4);
+                        half2 lo, hi;
+                        i8x4_to_h2(vv, lo, hi);
+                        const float2 a = __half22float2(lo);
+                        const float2 b = __half22float2(hi);
+                        vf[0] = a.x; vf[1] = a.y; vf[2] = b.x; vf[3] = b.y;
+                    }
+                    const float* pr = pbuf + t * HB;
+#pragma unroll
+                    for (int h = 0; h < HB; ++h) {
+                        const float ph = pr[h];
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) acc[h][c] = fmaf(ph, vf[c], acc[h][c]);
+                    }
+                }
+            } else {
+                const int hw = lane >> 4;
+                const int l16 = lane & 15;
+                for (int t = hw; t < nval; t += 2) {
+                    const uint32_t vv = *reinterpret_cast<const uint32_t*>(sV + (wt0 + t) * ROWB + l16 * 4);
+                    half2 o[4];
+                    i4x8_to_h2<F::SIGNED>(vv, o);
+                    float vf[8];
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const float2 f = __half22float2(o[k]);
+                        vf[2 * k] = f.x;
+                        vf[2 * k + 1] = f.y;
+                    }
+                    const float* pr = pbuf + t * HB;
+#pragma unroll
+                    for (int h = 0; h < HB; ++h) {
+                        const float ph = pr[h];
+#pragma unroll
+                        for (int c = 0; c < 8; ++c) acc[h][c] = fmaf(ph, vf[c], acc[h][c]);
+                    }
+                }
+            }
+            __syncwarp();
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+
+        // ---------------- end of a unit segment: merge and emit ----------------
+        if (ti == p.tpu - 1 || i == te - 1) {
+            if (PVC == 8) {
+#pragma unroll
+                for (int h = 0; h < HB; ++h)
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) acc[h][c] += __shfl_xor_sync(kFull, acc[h][c], 16);
+            }
+            if (grp == 0 && prim) {
+                float* e = mlb + (w * HB + hh) * 3;
+                e[0] = m_run;
+                e[1] = l_run;
+                e[2] = z_run;
+            }
+            named_bar_sync(1, nct);
+#pragma unroll
+            for (int h = 0; h < HB; ++h) {
+                float M = -INFINITY;
+                for (int ww = 0; ww < kNCW; ++ww) M = fmaxf(M, mlb[(ww * HB + h) * 3]);
+                const float f = fast_exp2(mlb[(w * HB + h) * 3] - M);
+                float* dst = abuf + (w * HB + h) * kHeadDim;
+                if (PVC == 4) {
+                    *reinterpret_cast<float4*>(dst + lane * 4) =
+                        make_float4(acc[h][0] * f, acc[h][1] * f, acc[h][2] * f, acc[h][3] * f);
+                } else if (lane < 16) {
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        dst[lane * 8 + k] = acc[h][2 * k] * f;
+                        dst[lane * 8 + k + 4] = acc[h][2 * k + 1] * f;
+                    }
+                }
+            }
+            named_bar_sync(1, nct);
+            const bool whole = (seg_t0 == 0 && ti == p.tpu - 1);
+            const long long first_unit_of_cta = tb / p.tpu;
+            const long long slot = 2 * cta + (unit == first_unit_of_cta ? 0 : 1);
+            for (int o = tid; o < HB * kHeadDim; o += nct) {
+                const int h = o >> 7;
+                float M = -INFINITY;
+                for (int ww = 0; ww < kNCW; ++ww) M = fmaxf(M, mlb[(ww * HB + h) * 3]);
+                float L = 0.f, Z = 0.f, A = 0.f;
+                for (int ww = 0; ww < kNCW; ++ww) {
+                    const float* e = mlb + (ww * HB + h) * 3;
+                    const float f = fast_exp2(e[0] - M);
+                    L = fmaf(e[1], f, L);
+                    if (F::ZV) Z = fmaf(e[2], f, Z);
+                    A += abuf[(ww * HB + h) * kHeadDim + (o & 127)];
+                }
+                A += Z;
+                if (whole) {
+                    p.out[qoff + o] = __float2half_rn(A / L);
+                } else {
+                    float* sp = p.part + slot * SL;
+                    sp[o] = A;
+                    if ((o & 127) == 0) {
+                        sp[HB * kHeadDim + h] = M;
+                        sp[HB * kHeadDim + HB + h] = L;
+                    }
+                }
+            }
+            if (!whole) {
+                __threadfence();
+                named_bar_sync(1, nct);
+                const long long c_lo = owner_cta(unit * p.tpu, p.total_tiles, p.n_ctas);
+                const long long c_hi = owner_cta((unit + 1) * p.tpu - 1, p.total_tiles, p.n_ctas);
+                if (tid == 0) {
+                    const unsigned nseg = static_cast<unsigned>(c_hi - c_lo + 1);
+                    const unsigned old = atomicAdd(&p.counters[unit], 1u);
+                    const int last = (old == nseg - 1);
+                    if (last) p.counters[unit] = 0u;
+                    misc[1] = last;
+                }
+                named_bar_sync(1, nct);
+                if (misc[1]) {
+                    __threadfence();
+                    for (int o = tid; o < HB * kHeadDim; o += nct) {
+                        const int h = o >> 7;
+                        float M = -INFINITY;
+                        for (long long c2 = c_lo; c2 <= c_hi; ++c2) {
+                            const long long fu = cta_first_tile(c2, p.total_tiles, p.n_ctas) / p.tpu;
+                            const float* sp = p.part + (2 * c2 + (fu == unit ? 0 : 1)) * SL;
+                            M = fmaxf(M, __ldcg(sp + HB * kHeadDim + h));
+                        }
+                        float L = 0.f, A = 0.f;
+                        for (long long c2 = c_lo; c2 <= c_hi; ++c2) {
+                            const long long fu = cta_first_tile(c2, p.total_tiles, p.n_ctas) / p.tpu;
+                            const float* sp = p.part + (2 * c2 + (fu == unit ? 0 : 1)) * SL;
+                            const float f = fast_exp2(__ldcg(sp + HB * kHeadDim + h) - M);
+                            L = fmaf(__ldcg(sp + HB * kHeadDim + HB + h), f, L);
+                            A = fmaf(__ldcg(sp + o), f, A);
+                        }
+                        p.out[qoff + o] = __float2half_rn(A / L);
+                    }
+                }
+            }
+            named_bar_sync(1, nct);
+        }
+    }
+}
+
+// ---- host side ------------------------------------------------------------
+
+int heads_per_unit(int64_t group, int fmt) {
+    // Eight heads per unit need more registers than the INT8/INT4 paths have
+    // (168 per thread at 9 warps per SM); those formats split a group of 8
+    // into two units of 4.
+    if (group % 8 == 0 && fmt == kF16) return 8;
+    if (group % 4 == 0) return 4;
+    if (group % 2 == 0) return 2;
+    return 1;
+}
+
+size_t decode_workspace_bytes(int64_t batch, int64_t n_heads, int64_t n_kv_heads, int sm_count) {
+    if (batch <= 0 || n_kv_heads <= 0 || n_heads <= 0) return kWsErrBytes;
+    const int64_t g = n_heads / n_kv_heads;
+    size_t best = 0;
+    for (int fmt = kF16; fmt <= kI4Asym; ++fmt) {
+        const int hb = heads_per_unit(g, fmt);
+        const int64_t n_units = batch * n_kv_heads * (g / hb);
+        const size_t counters = align_up(static_cast<size_t>(n_units) * 4, 256);
+        const size_t slots = static_cast<size_t>(2) * sm_count * (hb * kHeadDim + 2 * hb) * 4;
+        best = std::max(best, kWsErrBytes + counters + slots);
+    }
+    return best;
+}
+
+namespace {
+
+template <int FMT, int HB>
+lik_status launch_t(const DecodeArgs& a, const DeviceInfo& di, cudaStream_t stream, std::string& err) {
+    using F = Fmt<FMT>;
+    constexpr int T = F::T;
+    DecodeParams p{};
+    p.q = static_cast<const __half*>(a.q);
+    p.out = static_cast<__half*>(a.out);
+    p.k = static_cast<const uint8_t*>(a.k);
+    p.v = static_cast<const uint8_t*>(a.v);
+    p.ks = static_cast<const __half*>(a.k_scale);
+    p.vs = static_cast<const __half*>(a.v_scale);
+    p.kz = static_cast<const __half*>(a.k_zero);
+    p.vz = static_cast<const __half*>(a.v_zero);
+    p.seqlen = a.seqlen;
+    p.kv_buf_len = a.kv_buf_len;
+    p.ng_buf = a.n_groups_buf;
+    p.n_heads = static_cast<int>(a.n_heads);
+    p.n_kv_heads = static_cast<int>(a.n_kv_heads);
+    const int64_t g = a.n_heads / a.n_kv_heads;
+    p.nhb = static_cast<int>(g / HB);
+    p.n_units = a.batch * a.n_kv_heads * p.nhb;
+    p.tpu = (a.seqlen + T - 1) / T;
+    p.total_tiles = p.n_units * p.tpu;
+    p.group_size = static_cast<int>(F::KG ? a.group_size : 1);
+    p.qscale = a.softmax_scale * kLog2e;
+
+    // Per-token scales ride the bulk copy when every tile's scale run is
+    // 16-byte aligned and a multiple of 16 bytes (rounded up to 8 tokens,
+    // which stays inside the slab because kv_buf_len % 8 == 0).
+    auto al16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
+    bool tok_bulk = (a.kv_buf_len % 8 == 0);
+    if (F::TOKK) tok_bulk = tok_bulk && al16(a.k_scale);
+    if (F::TOKV) tok_bulk = tok_bulk && al16(a.v_scale);
+    if (F::ZV) tok_bulk = tok_bulk && al16(a.v_zero);
+    p.tok_bulk = tok_bulk ? 1 : 0;
+    bool kg_smem = F::KG && a.group_size >= 32 && al16(a.k_scale) && (!F::ZK || al16(a.k_zero));
+    p.kg_smem = kg_smem ? 1 : 0;
+    p.ngt = kg_smem ? static_cast<int>(std::min<int64_t>(a.n_groups_buf, (T + a.group_size - 1) / a.group_size + 1)) : 0;
+
+    // stage layout
+    int off = 2 * T * F::ROWB;
+    p.off_v = T * F::ROWB;
+    p.off_ks = off;
+    if (F::TOKK) off += T * 2;
+    p.off_vs = off;
+    if (F::TOKV) off += T * 2;
+    p.off_vz = off;
+    if (F::ZV) off += T * 2;
+    p.off_kgs = off;
+    off += p.ngt * kHeadDim * 2;
+    p.off_kgz = off;
+    if (F::ZK) off += p.ngt * kHeadDim * 2;
+    p.stage_bytes = static_cast<int>(align_up(off, 128));
+
+    const int work = static_cast<int>(std::max<size_t>(static_cast<size_t>(kNCW) * (T / kNCW) * HB * 4,
+                                                       static_cast<size_t>(kNCW) * HB * kHeadDim * 4));
+    const int fixed = work + kNCW * HB * 3 * 4 + 64 + 2 * 8 * 8;
+    int nst = (di.max_smem_optin - fixed - 256) / p.stage_bytes;
+    nst = std::min(nst, 8);
+    if (nst < 2) {
+        err = "shared memory too small for two pipeline stages";
+        return LIK_ERR_UNSUPPORTED;
+    }
+    // Never more stages than one CTA can use.
+    p.nst = nst;
+    size_t o2 = static_cast<size_t>(nst) * p.stage_bytes;
+    p.off_work = static_cast<int>(o2);
+    o2 += work;
+    p.off_ml = static_cast<int>(o2);
+    o2 += kNCW * HB * 3 * 4;
+    o2 = align_up(o2, 16);
+    p.off_misc = static_cast<int>(o2);
+    o2 += 16;
+    o2 = align_up(o2, 8);
+    p.off_bar = static_cast<int>(o2);
+    o2 += 2 * nst * 8;
+    const size_t smem = o2;
+
+    p.n_ctas = static_cast<int>(std::min<long long>(p.total_tiles, di.sm_count));
+
+    uint8_t* ws = static_cast<uint8_t*>(a.workspace);
+    p.err = reinterpret_cast<int*>(ws);
+    p.counters = reinterpret_cast<unsigned*>(ws + kWsErrBytes);
+    p.part = reinterpret_cast<float*>(ws + kWsErrBytes + align_up(static_cast<size_t>(p.n_units) * 4, 256));
+    const size_t need = kWsErrBytes + align_up(static_cast<size_t>(p.n_units) * 4, 256) +
+                        static_cast<size_t>(2) * p.n_ctas * (HB * kHeadDim + 2 * HB) * 4;
+    if (a.workspace == nullptr || a.workspace_bytes < need) {
+        err = "workspace too small: need " + std::to_string(need) + " bytes";
+        return LIK_ERR_WORKSPACE;
+    }
+
+    auto kern = decode_kernel<FMT, HB>;
+    static std::once_flag once[64];
+    static cudaError_t attr_err[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int slot = dev & 63;
+    std::call_once(once[slot], [&] {
+        attr_err[slot] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, di.max_smem_optin);
+    });
+    if (attr_err[slot] != cudaSuccess) {
+        err = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(attr_err[slot]);
+        return LIK_ERR_CUDA;
+    }
+    kern<<<p.n_ctas, kThreads, smem, stream>>>(p);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        err = std::string("decode kernel launch: ") + cudaGetErrorString(e);
+        return LIK_ERR_CUDA;
+    }
+    return LIK_OK;
+}
+
+template <int FMT>
+lik_status launch_fmt(const DecodeArgs& a, const DeviceInfo& di, cudaStream_t s, std::string& err) {
+    switch (heads_per_unit(a.n_heads / a.n_kv_heads, FMT)) {
+        case 8:
+            if constexpr (FMT == kF16) return launch_t<FMT, 8>(a, di, s, err);
+            err = "internal: eight heads per unit is fp16-only";
+            return LIK_ERR_UNSUPPORTED;
+        case 4: return launch_t<FMT, 4>(a, di, s, err);
+        case 2: return launch_t<FMT, 2>(a, di, s, err);
+        default: return launch_t<FMT, 1>(a, di, s, err);
+    }
+}
+
+}  // namespace
+
+lik_status launch_decode(const DecodeArgs& a, cudaStream_t stream, std::string& err) {
+    DeviceInfo di;
+    if (!device_info(di, err)) return LIK_ERR_CUDA;
+    switch (a.fmt) {
+        case kF16: return launch_fmt<kF16>(a, di, stream, err);
+        case kI8: return launch_fmt<kI8>(a, di, stream, err);
+        case kI4Sym: return launch_fmt<kI4Sym>(a, di, stream, err);
+        case kI4Asym: return launch_fmt<kI4Asym>(a, di, stream, err);
+        default: err = "unknown KV format"; return LIK_ERR_INVALID_ARGUMENT;
+    }
+}
+
+}  // namespace lik

@@ -1,0 +1,289 @@
+// KV quantize / pack kernels for sm_100a, bit-exact with the reference's
+// PyTorch oracle (reference/kv_cache_ref.py:46-62, 73-112) on fp16 inputs
+// viewed as fp32:
+//   scale = max(absmax / qmax, 1e-8)        IEEE fp32 division
+//   code  = clamp(rint(x / scale), +-qmax)  IEEE division, round half to even
+//   stored scale = fp16(scale)              round to nearest even
+// This translation unit is compiled without --use_fast_math and with
+// -fmad=false; divisions go through __fdiv_rn explicitly.
+//
+// The reference CUDA kernels (kernels/kv_cache/kv_compress.cu) multiply by a
+// reciprocal instead and differ from the oracle by one code at ~6e-5 of
+// positions; these kernels do not.
+//
+// Every kernel writes into a destination cache of allocated length
+// dst_buf_len at position dst_pos, so the same code serves the reference's
+// one-shot ops (dst_pos = 0, dst_buf_len = n_tokens) and in-place append into a
+// preallocated cache.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "lik_device.cuh"
+#include "lik_internal.h"
+
+namespace lik {
+
+namespace {
+
+constexpr float kAsymScaleFloor = 5.9604644775390625e-8f;  // 2^-24, smallest fp16 subnormal
+
+__device__ __forceinline__ void load8(const __half* src, float (&f)[8]) {
+    const uint4 u = *reinterpret_cast<const uint4*>(src);
+    const __half* h = reinterpret_cast<const __half*>(&u);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = __half2float(h[i]);
+}
+
+__device__ __forceinline__ uint32_t pack_nibbles8(const int (&c)[8]) {
+    uint32_t w = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) w |= (static_cast<uint32_t>(c[i]) & 0xFu) << (4 * i);
+    return w;
+}
+
+// One 16-lane half-warp per token row (8 channels per lane).
+// MODE kTokI8: int8 codes; kTokI4Sym: packed signed nibbles; kTokI4Asym:
+// packed unsigned nibbles with a zero point.
+template <int MODE>
+__global__ void __launch_bounds__(256) quant_token_kernel(const __half* __restrict__ x, uint8_t* __restrict__ codes,
+                                                          __half* __restrict__ scale, __half* __restrict__ zero,
+                                                          long long n_rows, long long n_tok, long long dst_pos,
+                                                          long long dst_buf) {
+    const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 4;
+    if (row >= n_rows) return;  // whole 16-lane groups leave together
+    const int l = threadIdx.x & 15;
+    const unsigned mask = 0xFFFFu << (threadIdx.x & 16);
+    float f[8];
+    load8(x + row * kHeadDim + l * 8, f);
+
+    const long long slab = row / n_tok;
+    const long long t = row - slab * n_tok;
+    const long long drow = slab * dst_buf + dst_pos + t;
+
+    if (MODE == kTokI4Asym) {
+        float mn = f[0], mx = f[0];
+#pragma unroll
+        for (int i = 1; i < 8; ++i) {
+            mn = fminf(mn, f[i]);
+            mx = fmaxf(mx, f[i]);
+        }
+#pragma unroll
+        for (int m = 1; m < 16; m <<= 1) {
+            mn = fminf(mn, __shfl_xor_sync(mask, mn, m));
+            mx = fmaxf(mx, __shfl_xor_sync(mask, mx, m));
+        }
+        const float s = fmaxf(__fdiv_rn(__fsub_rn(mx, mn), 15.0f), kAsymScaleFloor);
+        const __half sh = __float2half_rn(s);
+        const __half zh = __float2half_rn(mn);
+        const float sf = __half2float(sh);
+        const float zf = __half2float(zh);
+        int c[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float qv = rintf(__fdiv_rn(__fsub_rn(f[i], zf), sf));
+            c[i] = static_cast<int>(fminf(fmaxf(qv, 0.0f), 15.0f));
+        }
+        reinterpret_cast<uint32_t*>(codes + drow * (kHeadDim / 2))[l] = pack_nibbles8(c);
+        if (l == 0) {
+            scale[drow] = sh;
+            zero[drow] = zh;
+        }
+        return;
+    }
+
+    constexpr float qmax = (MODE == kTokI8) ? 127.0f : 7.0f;
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(f[i]));
+#pragma unroll
+    for (int m = 1; m < 16; m <<= 1) amax = fmaxf(amax, __shfl_xor_sync(mask, amax, m));
+    const float s = fmaxf(__fdiv_rn(amax, qmax), 1e-8f);
+    int c[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float qv = rintf(__fdiv_rn(f[i], s));
+        c[i] = static_cast<int>(fminf(fmaxf(qv, -qmax), qmax));
+    }
+    if (MODE == kTokI8) {
+        uint32_t lo = 0, hi = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            lo |= (static_cast<uint32_t>(c[i]) & 0xFFu) << (8 * i);
+            hi |= (static_cast<uint32_t>(c[4 + i]) & 0xFFu) << (8 * i);
+        }
+        reinterpret_cast<uint2*>(codes + drow * kHeadDim)[l] = make_uint2(lo, hi);
+    } else {
+        reinterpret_cast<uint32_t*>(codes + drow * (kHeadDim / 2))[l] = pack_nibbles8(c);
+    }
+    if (l == 0) scale[drow] = __float2half_rn(s);
+}
+
+// One CTA per (slab, token group): 16 channel chunks x 16 token lanes.
+// Pass 1 reduces each channel over the group's tokens; pass 2 re-reads the
+// group (L1/L2 resident) and writes packed codes.
+template <bool ASYM>
+__global__ void __launch_bounds__(256) quant_kgroup_kernel(const __half* __restrict__ x, uint8_t* __restrict__ codes,
+                                                           __half* __restrict__ scale, __half* __restrict__ zero,
+                                                           long long n_groups_new, long long n_tok, int gs,
+                                                           long long dst_pos, long long dst_buf, long long ng_buf) {
+    __shared__ float red_a[16][kHeadDim];
+    __shared__ float red_b[16][kHeadDim];
+    __shared__ float s_scale[kHeadDim];
+    __shared__ float s_zero[kHeadDim];
+
+    const long long blk = blockIdx.x;
+    const long long slab = blk / n_groups_new;
+    const long long g = blk - slab * n_groups_new;
+    const int cc = threadIdx.x & 15;
+    const int tl = threadIdx.x >> 4;
+    const long long t0 = g * gs;
+    const long long t1 = min(t0 + gs, n_tok);
+    const __half* xs = x + slab * n_tok * kHeadDim;
+
+    float a[8], b[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        a[i] = ASYM ? INFINITY : 0.0f;  // min (asym) or absmax (sym)
+        b[i] = -INFINITY;               // max (asym)
+    }
+    for (long long t = t0 + tl; t < t1; t += 16) {
+        float f[8];
+        load8(xs + t * kHeadDim + cc * 8, f);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            if (ASYM) {
+                a[i] = fminf(a[i], f[i]);
+                b[i] = fmaxf(b[i], f[i]);
+            } else {
+                a[i] = fmaxf(a[i], fabsf(f[i]));
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        red_a[tl][cc * 8 + i] = a[i];
+        if (ASYM) red_b[tl][cc * 8 + i] = b[i];
+    }
+    __syncthreads();
+    if (threadIdx.x < kHeadDim) {
+        const int ch = threadIdx.x;
+        float ra = red_a[0][ch], rb = ASYM ? red_b[0][ch] : 0.0f;
+        for (int r = 1; r < 16; ++r) {
+            if (ASYM) {
+                ra = fminf(ra, red_a[r][ch]);
+                rb = fmaxf(rb, red_b[r][ch]);
+            } else {
+                ra = fmaxf(ra, red_a[r][ch]);
+            }
+        }
+        const long long gidx = (slab * ng_buf + dst_pos / gs + g) * kHeadDim + ch;
+        if (ASYM) {
+            const float s = fmaxf(__fdiv_rn(__fsub_rn(rb, ra), 15.0f), kAsymScaleFloor);
+            const __half sh = __float2half_rn(s);
+            const __half zh = __float2half_rn(ra);
+            s_scale[ch] = __half2float(sh);
+            s_zero[ch] = __half2float(zh);
+            scale[gidx] = sh;
+            zero[gidx] = zh;
+        } else {
+            const float s = fmaxf(__fdiv_rn(ra, 7.0f), 1e-8f);
+            s_scale[ch] = s;
+            scale[gidx] = __float2half_rn(s);
+        }
+    }
+    __syncthreads();
+    float sc[8], zc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        sc[i] = s_scale[cc * 8 + i];
+        zc[i] = ASYM ? s_zero[cc * 8 + i] : 0.0f;
+    }
+    uint8_t* dst = codes + (slab * dst_buf + dst_pos) * (kHeadDim / 2);
+    for (long long t = t0 + tl; t < t1; t += 16) {
+        float f[8];
+        load8(xs + t * kHeadDim + cc * 8, f);
+        int c[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            if (ASYM) {
+                const float qv = rintf(__fdiv_rn(__fsub_rn(f[i], zc[i]), sc[i]));
+                c[i] = static_cast<int>(fminf(fmaxf(qv, 0.0f), 15.0f));
+            } else {
+                const float qv = rintf(__fdiv_rn(f[i], sc[i]));
+                c[i] = static_cast<int>(fminf(fmaxf(qv, -7.0f), 7.0f));
+            }
+        }
+        reinterpret_cast<uint32_t*>(dst + t * (kHeadDim / 2))[cc] = pack_nibbles8(c);
+    }
+}
+
+}  // namespace
+
+lik_status launch_quant_token(int mode, const void* x, void* codes, void* scale, void* zero, int64_t n_slabs,
+                              int64_t n_tokens, int64_t dst_pos, int64_t dst_buf_len, cudaStream_t stream,
+                              std::string& err) {
+    const long long n_rows = static_cast<long long>(n_slabs) * n_tokens;
+    if (n_rows == 0) return LIK_OK;
+    const long long blocks = (n_rows + 15) / 16;
+    if (blocks > 0x7fffffffLL) {
+        err = "too many rows";
+        return LIK_ERR_INVALID_ARGUMENT;
+    }
+    const __half* xh = static_cast<const __half*>(x);
+    uint8_t* c = static_cast<uint8_t*>(codes);
+    __half* s = static_cast<__half*>(scale);
+    __half* z = static_cast<__half*>(zero);
+    switch (mode) {
+        case kTokI8:
+            quant_token_kernel<kTokI8><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(xh, c, s, z, n_rows, n_tokens,
+                                                                                         dst_pos, dst_buf_len);
+            break;
+        case kTokI4Sym:
+            quant_token_kernel<kTokI4Sym><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+                xh, c, s, z, n_rows, n_tokens, dst_pos, dst_buf_len);
+            break;
+        default:
+            quant_token_kernel<kTokI4Asym><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+                xh, c, s, z, n_rows, n_tokens, dst_pos, dst_buf_len);
+            break;
+    }
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        err = std::string("quantize launch: ") + cudaGetErrorString(e);
+        return LIK_ERR_CUDA;
+    }
+    return LIK_OK;
+}
+
+lik_status launch_quant_kgroup(bool asym, const void* x, void* codes, void* scale, void* zero, int64_t n_slabs,
+                               int64_t n_tokens, int64_t group_size, int64_t dst_pos, int64_t dst_buf_len,
+                               int64_t n_groups_buf, cudaStream_t stream, std::string& err) {
+    const long long ngn = (n_tokens + group_size - 1) / group_size;
+    const long long blocks = static_cast<long long>(n_slabs) * ngn;
+    if (blocks == 0) return LIK_OK;
+    if (blocks > 0x7fffffffLL) {
+        err = "too many groups";
+        return LIK_ERR_INVALID_ARGUMENT;
+    }
+    const __half* xh = static_cast<const __half*>(x);
+    uint8_t* c = static_cast<uint8_t*>(codes);
+    __half* s = static_cast<__half*>(scale);
+    __half* z = static_cast<__half*>(zero);
+    if (asym) {
+        quant_kgroup_kernel<true><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+            xh, c, s, z, ngn, n_tokens, static_cast<int>(group_size), dst_pos, dst_buf_len, n_groups_buf);
+    } else {
+        quant_kgroup_kernel<false><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+            xh, c, s, z, ngn, n_tokens, static_cast<int>(group_size), dst_pos, dst_buf_len, n_groups_buf);
+    }
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        err = std::string("quantize launch: ") + cudaGetErrorString(e);
+        return LIK_ERR_CUDA;
+    }
+    return LIK_OK;
+}
+
+}  // namespace lik

@@ -1,0 +1,386 @@
+// `llmik_cuda._C`: the PyTorch op surface of the reference extension
+// (bindings/extension.cpp:476-494), rebuilt on the C ABI of
+// libllmik_b200.so (include/llmik.h).
+//
+// This layer only validates tensors (the reference's TORCH_CHECK
+// preconditions, plus head_dim == 128 and n_heads % n_kv_heads == 0 on every
+// op), allocates outputs with the caching allocator, picks the current stream
+// and turns a lik_status into a Python RuntimeError. All arithmetic is in the
+// CUDA library; there is no CPU path.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <map>
+#include <mutex>
+#include <tuple>
+
+#include "llmik.h"
+
+namespace {
+
+void ok_or_throw(lik_status s, const char* op) {
+    TORCH_CHECK(s == LIK_OK, op, ": ", lik_status_string(s), ": ", lik_last_error());
+}
+
+void* cur_stream() { return static_cast<void*>(at::cuda::getCurrentCUDAStream().stream()); }
+
+// One zero-initialised workspace per (device, stream), grown on demand. Kept
+// alive for the life of the process so repeated decode steps (and CUDA-graph
+// replays) reuse it; the kernels leave it zeroed after every call.
+at::Tensor& workspace(const at::Tensor& like, size_t bytes) {
+    static std::mutex mu;
+    static std::map<std::pair<int, void*>, at::Tensor> cache;
+    std::lock_guard<std::mutex> lock(mu);
+    auto key = std::make_pair(static_cast<int>(like.get_device()), cur_stream());
+    at::Tensor& t = cache[key];
+    if (!t.defined() || static_cast<size_t>(t.numel()) < bytes) {
+        t = torch::empty({static_cast<int64_t>(bytes)}, like.options().dtype(torch::kUInt8));
+        ok_or_throw(lik_workspace_init(t.data_ptr(), bytes, cur_stream()), "workspace init");
+    }
+    return t;
+}
+
+void check_cuda(const at::Tensor& t, const char* name) {
+    TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+    TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+}
+
+void check_q(const at::Tensor& q) {
+    check_cuda(q, "q");
+    TORCH_CHECK(q.scalar_type() == torch::kHalf, "q must be fp16");
+    TORCH_CHECK(q.dim() == 3, "q must be [batch, n_heads, head_dim]");
+    TORCH_CHECK(q.size(2) == 128, "only head_dim=128 supported");
+}
+
+void check_kv4(const at::Tensor& t, const char* name, at::ScalarType dt, int64_t last) {
+    check_cuda(t, name);
+    TORCH_CHECK(t.scalar_type() == dt, name, " has the wrong dtype");
+    TORCH_CHECK(t.dim() == 4, name, " must be [batch, n_kv_heads, seqlen, ", last, "]");
+    TORCH_CHECK(t.size(3) == last, name, " last dim must be ", last);
+}
+
+void check_same_device(const at::Tensor& a, const at::Tensor& b) {
+    TORCH_CHECK(a.device() == b.device(), "all tensors must be on the same device");
+}
+
+int64_t live_len(int64_t seqlen, int64_t buf) {
+    const int64_t s = seqlen > 0 ? seqlen : buf;
+    TORCH_CHECK(s <= buf, "seqlen exceeds allocated cache length");
+    return s;
+}
+
+void check_heads(const at::Tensor& q, const at::Tensor& k) {
+    TORCH_CHECK(k.size(0) == q.size(0), "batch mismatch between q and the KV cache");
+    TORCH_CHECK(k.size(1) > 0 && q.size(1) % k.size(1) == 0, "n_heads must be a multiple of n_kv_heads");
+}
+
+void check_tok_scale(const at::Tensor& s, const at::Tensor& codes, const char* name) {
+    check_cuda(s, name);
+    TORCH_CHECK(s.scalar_type() == torch::kHalf, name, " must be fp16");
+    TORCH_CHECK(s.dim() == 3 && s.size(0) == codes.size(0) && s.size(1) == codes.size(1) &&
+                    s.size(2) == codes.size(2),
+                name, " must be [batch, n_kv_heads, seqlen]");
+}
+
+void check_group_scale(const at::Tensor& s, const at::Tensor& codes, const char* name) {
+    check_cuda(s, name);
+    TORCH_CHECK(s.scalar_type() == torch::kHalf, name, " must be fp16");
+    TORCH_CHECK(s.dim() == 4 && s.size(0) == codes.size(0) && s.size(1) == codes.size(1) && s.size(3) == 128,
+                name, " must be [batch, n_kv_heads, n_groups, head_dim]");
+}
+
+// ---------------------------------------------------------------- attention
+
+torch::Tensor decode_attention(torch::Tensor q, torch::Tensor k, torch::Tensor v, double softmax_scale,
+                               int64_t seqlen) {
+    check_q(q);
+    check_kv4(k, "k", torch::kHalf, 128);
+    check_kv4(v, "v", torch::kHalf, 128);
+    TORCH_CHECK(k.sizes() == v.sizes(), "k and v must have the same shape");
+    check_same_device(q, k);
+    check_same_device(q, v);
+    check_heads(q, k);
+    const c10::cuda::CUDAGuard guard(q.device());
+    const int64_t buf = k.size(2);
+    const int64_t s = live_len(seqlen, buf);
+    auto out = torch::empty_like(q);
+    const size_t wb = lik_decode_workspace_bytes(q.size(0), q.size(1), k.size(1));
+    at::Tensor& ws = workspace(q, wb);
+    ok_or_throw(lik_decode_attention_f16(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), q.size(0),
+                                         q.size(1), k.size(1), q.size(2), s, buf,
+                                         static_cast<float>(softmax_scale), ws.data_ptr(), ws.numel(),
+                                         cur_stream()),
+                "decode_attention");
+    return out;
+}
+
+torch::Tensor decode_attention_v3(torch::Tensor q, torch::Tensor k, torch::Tensor v, double softmax_scale) {
+    // The reference's single-warp v3 kernel has no separate implementation
+    // here: the same split-sequence kernel serves every length.
+    return decode_attention(q, k, v, softmax_scale, -1);
+}
+
+torch::Tensor decode_attention_int8(torch::Tensor q, torch::Tensor k_q, torch::Tensor k_scale, torch::Tensor v_q,
+                                    torch::Tensor v_scale, double softmax_scale, int64_t seqlen) {
+    check_q(q);
+    check_kv4(k_q, "k_q", torch::kInt8, 128);
+    check_kv4(v_q, "v_q", torch::kInt8, 128);
+    TORCH_CHECK(k_q.sizes() == v_q.sizes(), "k_q and v_q must have the same shape");
+    check_tok_scale(k_scale, k_q, "k_scale");
+    check_tok_scale(v_scale, v_q, "v_scale");
+    for (auto* t : {&k_q, &v_q, &k_scale, &v_scale}) check_same_device(q, *t);
+    check_heads(q, k_q);
+    const c10::cuda::CUDAGuard guard(q.device());
+    const int64_t buf = k_q.size(2);
+    const int64_t s = live_len(seqlen, buf);
+    auto out = torch::empty_like(q);
+    at::Tensor& ws = workspace(q, lik_decode_workspace_bytes(q.size(0), q.size(1), k_q.size(1)));
+    ok_or_throw(lik_decode_attention_int8(q.data_ptr(), k_q.data_ptr<int8_t>(), k_scale.data_ptr(),
+                                          v_q.data_ptr<int8_t>(), v_scale.data_ptr(), out.data_ptr(), q.size(0),
+                                          q.size(1), k_q.size(1), q.size(2), s, buf,
+                                          static_cast<float>(softmax_scale), ws.data_ptr(), ws.numel(),
+                                          cur_stream()),
+                "decode_attention_int8");
+    return out;
+}
+
+torch::Tensor decode_attention_int4(torch::Tensor q, torch::Tensor k_q, torch::Tensor k_scale, torch::Tensor v_q,
+                                    torch::Tensor v_scale, int64_t group_size, double softmax_scale,
+                                    int64_t seqlen) {
+    check_q(q);
+    check_kv4(k_q, "k_q", torch::kInt8, 64);
+    check_kv4(v_q, "v_q", torch::kInt8, 64);
+    TORCH_CHECK(k_q.sizes() == v_q.sizes(), "k_q and v_q must have the same shape");
+    check_group_scale(k_scale, k_q, "k_scale");
+    check_tok_scale(v_scale, v_q, "v_scale");
+    TORCH_CHECK(group_size > 0, "group_size must be positive");
+    for (auto* t : {&k_q, &v_q, &k_scale, &v_scale}) check_same_device(q, *t);
+    check_heads(q, k_q);
+    const c10::cuda::CUDAGuard guard(q.device());
+    const int64_t buf = k_q.size(2);
+    const int64_t s = live_len(seqlen, buf);
+    auto out = torch::empty_like(q);
+    at::Tensor& ws = workspace(q, lik_decode_workspace_bytes(q.size(0), q.size(1), k_q.size(1)));
+    ok_or_throw(lik_decode_attention_int4(q.data_ptr(), k_q.data_ptr<int8_t>(), k_scale.data_ptr(),
+                                          v_q.data_ptr<int8_t>(), v_scale.data_ptr(), out.data_ptr(), q.size(0),
+                                          q.size(1), k_q.size(1), q.size(2), s, buf, group_size, k_scale.size(2),
+                                          static_cast<float>(softmax_scale), ws.data_ptr(), ws.numel(),
+                                          cur_stream()),
+                "decode_attention_int4");
+    return out;
+}
+
+torch::Tensor decode_attention_int4_asym(torch::Tensor q, torch::Tensor k_q, torch::Tensor k_scale,
+                                         torch::Tensor k_zero, torch::Tensor v_q, torch::Tensor v_scale,
+                                         torch::Tensor v_zero, int64_t group_size, double softmax_scale,
+                                         int64_t seqlen) {
+    check_q(q);
+    check_kv4(k_q, "k_q", torch::kInt8, 64);
+    check_kv4(v_q, "v_q", torch::kInt8, 64);
+    TORCH_CHECK(k_q.sizes() == v_q.sizes(), "k_q and v_q must have the same shape");
+    check_group_scale(k_scale, k_q, "k_scale");
+    check_group_scale(k_zero, k_q, "k_zero");
+    TORCH_CHECK(k_zero.sizes() == k_scale.sizes(), "k_zero must match k_scale");
+    check_tok_scale(v_scale, v_q, "v_scale");
+    check_tok_scale(v_zero, v_q, "v_zero");
+    TORCH_CHECK(group_size > 0, "group_size must be positive");
+    for (auto* t : {&k_q, &v_q, &k_scale, &v_scale, &k_zero, &v_zero}) check_same_device(q, *t);
+    check_heads(q, k_q);
+    const c10::cuda::CUDAGuard guard(q.device());
+    const int64_t buf = k_q.size(2);
+    const int64_t s = live_len(seqlen, buf);
+    auto out = torch::empty_like(q);
+    at::Tensor& ws = workspace(q, lik_decode_workspace_bytes(q.size(0), q.size(1), k_q.size(1)));
+    ok_or_throw(lik_decode_attention_int4_asym(
+                    q.data_ptr(), k_q.data_ptr<int8_t>(), k_scale.data_ptr(), k_zero.data_ptr(),
+                    v_q.data_ptr<int8_t>(), v_scale.data_ptr(), v_zero.data_ptr(), out.data_ptr(), q.size(0),
+                    q.size(1), k_q.size(1), q.size(2), s, buf, group_size, k_scale.size(2),
+                    static_cast<float>(softmax_scale), ws.data_ptr(), ws.numel(), cur_stream()),
+                "decode_attention_int4_asym");
+    return out;
+}
+
+// ---------------------------------------------------------------- quantize
+
+void check_x(const at::Tensor& x) {
+    check_cuda(x, "x");
+    TORCH_CHECK(x.scalar_type() == torch::kHalf, "x must be fp16");
+    TORCH_CHECK(x.dim() == 4, "x must be [batch, n_kv_heads, seqlen, head_dim]");
+    TORCH_CHECK(x.size(3) == 128, "only head_dim=128 supported");
+}
+
+std::tuple<torch::Tensor, torch::Tensor> quantize_per_token(torch::Tensor x) {
+    check_x(x);
+    const c10::cuda::CUDAGuard guard(x.device());
+    const auto B = x.size(0), H = x.size(1), S = x.size(2);
+    auto q = torch::empty({B, H, S, 128}, x.options().dtype(torch::kInt8));
+    auto s = torch::empty({B, H, S}, x.options().dtype(torch::kHalf));
+    ok_or_throw(lik_quantize_per_token_int8(x.data_ptr(), q.data_ptr<int8_t>(), s.data_ptr(), B, H, S, 128, 0, S,
+                                            cur_stream()),
+                "quantize_per_token");
+    return {q, s};
+}
+
+std::tuple<torch::Tensor, torch::Tensor> quantize_v_per_token_int4(torch::Tensor x) {
+    check_x(x);
+    const c10::cuda::CUDAGuard guard(x.device());
+    const auto B = x.size(0), H = x.size(1), S = x.size(2);
+    auto q = torch::empty({B, H, S, 64}, x.options().dtype(torch::kInt8));
+    auto s = torch::empty({B, H, S}, x.options().dtype(torch::kHalf));
+    ok_or_throw(lik_quantize_v_per_token_int4(x.data_ptr(), q.data_ptr<int8_t>(), s.data_ptr(), B, H, S, 128, 0,
+                                              S, cur_stream()),
+                "quantize_v_per_token_int4");
+    return {q, s};
+}
+
+std::tuple<torch::Tensor, torch::Tensor> quantize_k_per_channel_groupwise_int4(torch::Tensor x,
+                                                                                int64_t group_size) {
+    check_x(x);
+    TORCH_CHECK(group_size > 0, "group_size must be positive");
+    const c10::cuda::CUDAGuard guard(x.device());
+    const auto B = x.size(0), H = x.size(1), S = x.size(2);
+    const int64_t ng = (S + group_size - 1) / group_size;
+    auto q = torch::empty({B, H, S, 64}, x.options().dtype(torch::kInt8));
+    auto s = torch::empty({B, H, ng, 128}, x.options().dtype(torch::kHalf));
+    ok_or_throw(lik_quantize_k_per_channel_groupwise_int4(x.data_ptr(), q.data_ptr<int8_t>(), s.data_ptr(), B, H,
+                                                          S, 128, group_size, 0, S, ng, cur_stream()),
+                "quantize_k_per_channel_groupwise_int4");
+    return {q, s};
+}
+
+std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> quantize_v_per_token_int4_asym(torch::Tensor x) {
+    check_x(x);
+    const c10::cuda::CUDAGuard guard(x.device());
+    const auto B = x.size(0), H = x.size(1), S = x.size(2);
+    auto q = torch::empty({B, H, S, 64}, x.options().dtype(torch::kInt8));
+    auto s = torch::empty({B, H, S}, x.options().dtype(torch::kHalf));
+    auto z = torch::empty({B, H, S}, x.options().dtype(torch::kHalf));
+    ok_or_throw(lik_quantize_v_per_token_int4_asym(x.data_ptr(), q.data_ptr<int8_t>(), s.data_ptr(), z.data_ptr(),
+                                                   B, H, S, 128, 0, S, cur_stream()),
+                "quantize_v_per_token_int4_asym");
+    return {q, s, z};
+}
+
+std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> quantize_k_per_channel_groupwise_int4_asym(
+    torch::Tensor x, int64_t group_size) {
+    check_x(x);
+    TORCH_CHECK(group_size > 0, "group_size must be positive");
+    const c10::cuda::CUDAGuard guard(x.device());
+    const auto B = x.size(0), H = x.size(1), S = x.size(2);
+    const int64_t ng = (S + group_size - 1) / group_size;
+    auto q = torch::empty({B, H, S, 64}, x.options().dtype(torch::kInt8));
+    auto s = torch::empty({B, H, ng, 128}, x.options().dtype(torch::kHalf));
+    auto z = torch::empty({B, H, ng, 128}, x.options().dtype(torch::kHalf));
+    ok_or_throw(lik_quantize_k_per_channel_groupwise_int4_asym(x.data_ptr(), q.data_ptr<int8_t>(), s.data_ptr(),
+                                                               z.data_ptr(), B, H, S, 128, group_size, 0, S, ng,
+                                                               cur_stream()),
+                "quantize_k_per_channel_groupwise_int4_asym");
+    return {q, s, z};
+}
+
+// ------------------------------------------------ append into a preallocated cache
+//
+// x [B, Hkv, n, 128] fp16 is quantized into rows [pos, pos + n) of a cache
+// whose codes are [B, Hkv, buf_len, 128 or 64] and per-token scales
+// [B, Hkv, buf_len] (per-group K scales [B, Hkv, n_groups_buf, 128]).
+
+void check_cache(const at::Tensor& x, const at::Tensor& codes, int64_t last, int64_t pos) {
+    check_x(x);
+    check_kv4(codes, "codes", torch::kInt8, last);
+    check_same_device(x, codes);
+    TORCH_CHECK(codes.size(0) == x.size(0) && codes.size(1) == x.size(1), "cache batch/heads mismatch");
+    TORCH_CHECK(pos >= 0 && pos + x.size(2) <= codes.size(2), "append overflows the cache");
+}
+
+void quantize_per_token_into(torch::Tensor x, torch::Tensor codes, torch::Tensor scale, int64_t pos) {
+    check_cache(x, codes, 128, pos);
+    check_tok_scale(scale, codes, "scale");
+    const c10::cuda::CUDAGuard guard(x.device());
+    ok_or_throw(lik_quantize_per_token_int8(x.data_ptr(), codes.data_ptr<int8_t>(), scale.data_ptr(), x.size(0),
+                                            x.size(1), x.size(2), 128, pos, codes.size(2), cur_stream()),
+                "quantize_per_token_into");
+}
+
+void quantize_v_per_token_int4_into(torch::Tensor x, torch::Tensor codes, torch::Tensor scale, int64_t pos,
+                                    c10::optional<torch::Tensor> zero) {
+    check_cache(x, codes, 64, pos);
+    check_tok_scale(scale, codes, "scale");
+    const c10::cuda::CUDAGuard guard(x.device());
+    lik_status st;
+    if (zero.has_value()) {
+        check_tok_scale(*zero, codes, "zero");
+        st = lik_quantize_v_per_token_int4_asym(x.data_ptr(), codes.data_ptr<int8_t>(), scale.data_ptr(),
+                                                zero->data_ptr(), x.size(0), x.size(1), x.size(2), 128, pos,
+                                                codes.size(2), cur_stream());
+    } else {
+        st = lik_quantize_v_per_token_int4(x.data_ptr(), codes.data_ptr<int8_t>(), scale.data_ptr(), x.size(0),
+                                           x.size(1), x.size(2), 128, pos, codes.size(2), cur_stream());
+    }
+    ok_or_throw(st, "quantize_v_per_token_int4_into");
+}
+
+void quantize_k_per_channel_groupwise_int4_into(torch::Tensor x, torch::Tensor codes, torch::Tensor scale,
+                                                int64_t group_size, int64_t pos,
+                                                c10::optional<torch::Tensor> zero) {
+    check_cache(x, codes, 64, pos);
+    check_group_scale(scale, codes, "scale");
+    TORCH_CHECK(group_size > 0, "group_size must be positive");
+    const c10::cuda::CUDAGuard guard(x.device());
+    lik_status st;
+    if (zero.has_value()) {
+        check_group_scale(*zero, codes, "zero");
+        st = lik_quantize_k_per_channel_groupwise_int4_asym(x.data_ptr(), codes.data_ptr<int8_t>(),
+                                                            scale.data_ptr(), zero->data_ptr(), x.size(0),
+                                                            x.size(1), x.size(2), 128, group_size, pos,
+                                                            codes.size(2), scale.size(2), cur_stream());
+    } else {
+        st = lik_quantize_k_per_channel_groupwise_int4(x.data_ptr(), codes.data_ptr<int8_t>(), scale.data_ptr(),
+                                                       x.size(0), x.size(1), x.size(2), 128, group_size, pos,
+                                                       codes.size(2), scale.size(2), cur_stream());
+    }
+    ok_or_throw(st, "quantize_k_per_channel_groupwise_int4_into");
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+    namespace py = pybind11;
+    m.doc() = "B200 (sm_100a) GQA decode attention over fp16 / INT8 / INT4-KIVI KV caches";
+    m.def("decode_attention", &decode_attention,
+          "Decode attention over an fp16 KV cache (split-sequence, fused combine)", py::arg("q"), py::arg("k"),
+          py::arg("v"), py::arg("softmax_scale"), py::arg("seqlen") = -1);
+    m.def("decode_attention_v3", &decode_attention_v3, "Alias of decode_attention over the whole cache",
+          py::arg("q"), py::arg("k"), py::arg("v"), py::arg("softmax_scale"));
+    m.def("quantize_per_token", &quantize_per_token, "INT8 per-token symmetric KV quantization", py::arg("x"));
+    m.def("decode_attention_int8", &decode_attention_int8, "Decode attention over an INT8 per-token KV cache",
+          py::arg("q"), py::arg("k_q"), py::arg("k_scale"), py::arg("v_q"), py::arg("v_scale"),
+          py::arg("softmax_scale"), py::arg("seqlen") = -1);
+    m.def("quantize_k_per_channel_groupwise_int4", &quantize_k_per_channel_groupwise_int4,
+          "INT4 per-channel groupwise quantization (KIVI K), packed", py::arg("x"), py::arg("group_size"));
+    m.def("quantize_v_per_token_int4", &quantize_v_per_token_int4,
+          "INT4 per-token quantization (KIVI V), packed", py::arg("x"));
+    m.def("decode_attention_int4", &decode_attention_int4, "Decode attention over a KIVI INT4 KV cache",
+          py::arg("q"), py::arg("k_q"), py::arg("k_scale"), py::arg("v_q"), py::arg("v_scale"),
+          py::arg("group_size"), py::arg("softmax_scale"), py::arg("seqlen") = -1);
+    m.def("quantize_k_per_channel_groupwise_int4_asym", &quantize_k_per_channel_groupwise_int4_asym,
+          "Asymmetric INT4 per-channel groupwise quantization (scale + zero), packed", py::arg("x"),
+          py::arg("group_size"));
+    m.def("quantize_v_per_token_int4_asym", &quantize_v_per_token_int4_asym,
+          "Asymmetric INT4 per-token quantization (scale + zero), packed", py::arg("x"));
+    m.def("decode_attention_int4_asym", &decode_attention_int4_asym,
+          "Decode attention over an asymmetric INT4 KIVI KV cache", py::arg("q"), py::arg("k_q"),
+          py::arg("k_scale"), py::arg("k_zero"), py::arg("v_q"), py::arg("v_scale"), py::arg("v_zero"),
+          py::arg("group_size"), py::arg("softmax_scale"), py::arg("seqlen") = -1);
+    m.def("quantize_per_token_into", &quantize_per_token_into,
+          "INT8 per-token quantize of new tokens into a preallocated cache at pos", py::arg("x"),
+          py::arg("codes"), py::arg("scale"), py::arg("pos"));
+    m.def("quantize_v_per_token_int4_into", &quantize_v_per_token_int4_into,
+          "INT4 per-token quantize (zero given: asymmetric) into a preallocated cache at pos", py::arg("x"),
+          py::arg("codes"), py::arg("scale"), py::arg("pos"), py::arg("zero") = py::none());
+    m.def("quantize_k_per_channel_groupwise_int4_into", &quantize_k_per_channel_groupwise_int4_into,
+          "INT4 per-channel groupwise quantize (zero given: asymmetric) into a preallocated cache at pos "
+          "(a multiple of group_size)",
+          py::arg("x"), py::arg("codes"), py::arg("scale"), py::arg("group_size"), py::arg("pos"),
+          py::arg("zero") = py::none());
+}
