@@ -1,0 +1,563 @@
+"""Benchmark: single-query GQA decode over fp16 / INT8 / INT4-KIVI KV on B200.
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl ours|reference]
+
+Headline workload (one step = one decode-attention launch over one batch):
+BASELINE config 1 per GPU - batch 8, 32 query / 8 KV heads, head_dim 128,
+seqlen 4096, fp16 KV [B, Hkv, S, D] contiguous, seeded N(0,1) synthetic data.
+With N GPUs each rank runs its own config-1 batch (global batch 8N; units are
+(batch, kv-head) pairs, disjoint per rank, no collective on the hot path):
+"scaling": "weak". value = HBM bytes the step must move on all ranks (K + V
+codes + scales/zeros + q + out) / the max over ranks of the device time per
+step, in TB/s.
+
+Also reported on the same line: INT8 per-token (config 2), INT4 KIVI
+asymmetric g128 (config 3) and the reference's symmetric INT4 format at g128;
+config 4 (batch 64, seqlen 32768, fp16 and INT4 asym) sharded over the ranks
+by (batch, kv-head) (strong scaling of a fixed job); an end-to-end number
+through the public op with pinned host buffers; the roofline of the fp16
+kernel against the measured HBM peak; and the CPU oracle timed on this host.
+
+Timing: K steps are captured in one CUDA graph (each step reads a different
+copy of the inputs; the copies together exceed 3x the L2 size, so every step
+streams from HBM) and replayed once between CUDA events after a barrier and a
+synchronize; the max over ranks is reported.
+
+--impl reference times the reference's CPU path (the numpy port of
+reference/attention_ref.py in oracle/) on this host with all cores, one
+(batch, kv-head) unit of config 1 per step; rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "llm-inference-kernels_b200"))
+sys.path.insert(0, ROOT)
+
+HQ, HKV, D = 32, 8, 128
+C1 = dict(batch=8, seqlen=4096)
+C4 = dict(batch=64, seqlen=32768)
+GS = 128
+SCALE = 1.0 / math.sqrt(D)
+METRIC = "GQA decode achieved HBM TB/s (fp16 KV, config 1 per GPU)"
+
+
+def algo_bytes(fmt: str, batch: int, seqlen: int, gs: int = GS) -> int:
+    """Bytes one decode step must move: codes + scales/zeros + q + out."""
+    units = batch * HKV
+    qo = 2 * batch * HQ * D * 2
+    if fmt == "f16":
+        return units * seqlen * D * 2 * 2 + qo
+    if fmt == "int8":
+        return units * seqlen * (D + 2) * 2 + qo
+    ng = -(-seqlen // gs)
+    kv = units * seqlen * (D // 2) * 2
+    if fmt == "int4":
+        return kv + units * ng * D * 2 + units * seqlen * 2 + qo
+    if fmt == "int4_asym":
+        return kv + 2 * units * ng * D * 2 + 2 * units * seqlen * 2 + qo
+    raise ValueError(fmt)
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-c4", action="store_true", help="skip the config-4 lines")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    return ap.parse_args()
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+# --------------------------------------------------------------- CPU side
+
+def cpu_info():
+    model = ""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return model
+
+
+def cpu_unit_sample(steps: int, warmup: int):
+    """Time the CPU oracle on one (batch, kv-head) unit of config 1 per step.
+
+    Returns (seconds per unit, threads). numpy's BLAS uses all host cores.
+    """
+    import numpy as np
+    from oracle import kv_oracle as O
+
+    rng = np.random.default_rng(0)
+    g = HQ // HKV
+    q = rng.standard_normal((1, g, D)).astype(np.float16)
+    k = rng.standard_normal((1, 1, C1["seqlen"], D)).astype(np.float16)
+    v = rng.standard_normal((1, 1, C1["seqlen"], D)).astype(np.float16)
+    for _ in range(max(1, warmup)):
+        O.decode_attention(q, k, v, SCALE)
+    times = []
+    for _ in range(steps):
+        t = time.perf_counter()
+        O.decode_attention(q, k, v, SCALE)
+        times.append(time.perf_counter() - t)
+    return statistics.median(times), sum(times), os.cpu_count() or 1
+
+
+def unit_bytes_c1() -> float:
+    return algo_bytes("f16", C1["batch"], C1["seqlen"]) / (C1["batch"] * HKV)
+
+
+def run_reference(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    steps = args.steps
+    med, total, cores = cpu_unit_sample(steps, args.warmup)
+    tbs = unit_bytes_c1() / med / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": tbs, "unit": "TB/s",
+        "n_gpus": args.gpus, "steps": steps, "warmup": args.warmup,
+        "ms_per_step": med * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1), fp16)",
+        "config": {"workload": "config1 fp16 KV decode, 1 of 64 (batch, kv-head) units per step",
+                   "batch": C1["batch"], "n_heads": HQ, "n_kv_heads": HKV, "head_dim": D,
+                   "seqlen": C1["seqlen"]},
+        "cpu_baseline": {"value": tbs, "unit": "TB/s", "cores": cores, "kind": "port",
+                         "sample": "one (batch, kv-head) unit of config 1 (4 query heads, 4096 positions) "
+                                   "per step; numpy port of reference/attention_ref.py; " + cpu_info()},
+        "e2e": {"value": tbs, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# --------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling while the GPU is loaded."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------- GPU side
+
+def make_slabs(torch, dev, batch, seqlen, slab0, seed, outliers=False):
+    """K, V [batch, Hkv, seqlen, D] fp16, each (batch, kv-head) slab drawn from
+    its own generator seeded with seed + global slab index, so any rank can
+    regenerate any slab independently of the GPU count."""
+    k = torch.empty(batch, HKV, seqlen, D, dtype=torch.float16, device=dev)
+    v = torch.empty_like(k)
+    g = torch.Generator(device=dev)
+    for b in range(batch):
+        for h in range(HKV):
+            g.manual_seed(seed + slab0 + b * HKV + h)
+            kk = torch.randn(seqlen, D, generator=g, device=dev)
+            if outliers:   # config 3: 4 of 128 K channels scaled x10
+                kk[:, [0, 37, 74, 111]] *= 10.0
+            k[b, h] = kk.half()
+            v[b, h] = torch.randn(seqlen, D, generator=g, device=dev).half()
+    return k, v
+
+
+class Workload:
+    """R copies of one decode step's inputs for one KV format, and the op call."""
+
+    def __init__(self, torch, L, dev, fmt, batch, seqlen, slab0, copies, seed=1000):
+        self.fmt, self.batch, self.seqlen = fmt, batch, seqlen
+        self.sets = []
+        gq = torch.Generator(device=dev)
+        for r in range(copies):
+            base = seed + r * 1_000_003
+            gq.manual_seed(base + 7 * 10**6 + slab0)
+            q = torch.randn(batch, HQ, D, generator=gq, device=dev).half()
+            k, v = make_slabs(torch, dev, batch, seqlen, slab0, base, outliers=fmt.startswith("int4"))
+            if fmt == "f16":
+                args = (q, k, v)
+            elif fmt == "int8":
+                kq, ks = L.quantize_per_token(k)
+                vq, vs = L.quantize_per_token(v)
+                args = (q, kq, ks, vq, vs)
+            elif fmt == "int4":
+                kq, ks = L.quantize_k_per_channel_groupwise_int4(k, GS)
+                vq, vs = L.quantize_v_per_token_int4(v)
+                args = (q, kq, ks, vq, vs)
+            else:
+                kq, ks, kz = L.quantize_k_per_channel_groupwise_int4_asym(k, GS)
+                vq, vs, vz = L.quantize_v_per_token_int4_asym(v)
+                args = (q, kq, ks, kz, vq, vs, vz)
+            del k, v
+            self.sets.append(args)
+        self.L = L
+
+    def step(self, i):
+        a = self.sets[i % len(self.sets)]
+        L = self.L
+        if self.fmt == "f16":
+            return L.decode_attention(a[0], a[1], a[2], SCALE)
+        if self.fmt == "int8":
+            return L.decode_attention_int8(*a, SCALE)
+        if self.fmt == "int4":
+            return L.decode_attention_int4(*a, GS, SCALE)
+        return L.decode_attention_int4_asym(*a, GS, SCALE)
+
+    def bytes(self):
+        return algo_bytes(self.fmt, self.batch, self.seqlen)
+
+
+def copies_for(nbytes, l2):
+    return max(1, math.ceil(3 * l2 / nbytes))
+
+
+def time_graph(torch, wl, steps, warmup, barrier, min_warm_s=1.0):
+    """Capture `steps` steps in one CUDA graph; warm up; replay once timed.
+    Returns device ms per step on this rank."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for i in range(max(3, warmup)):
+            wl.step(i)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for i in range(steps):
+            wl.step(i)
+    # untimed replays: settle clocks and caches (at least min_warm_s)
+    t0 = time.perf_counter()
+    n = 0
+    while n < max(1, warmup) or time.perf_counter() - t0 < min_warm_s:
+        g.replay()
+        torch.cuda.synchronize()
+        n += 1
+        if n > 10000:
+            break
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(s):
+        e0.record(s)
+        g.replay()
+        e1.record(s)
+    torch.cuda.synchronize()
+    barrier()
+    del g
+    return e0.elapsed_time(e1) / steps
+
+
+def max_over_ranks(torch, x, world):
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def physical_index(local: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        parts = [x.strip() for x in vis.split(",") if x.strip()]
+        if local < len(parts) and parts[local].isdigit():
+            return int(parts[local])
+    return local
+
+
+def measured_hbm_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def ncu_traffic():
+    """Per-launch DRAM bytes of the fp16 config-1 kernel from the committed
+    ncu summary (profiles/decode_f16_config1.json), if present."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "decode_f16_config1.json")) as f:
+            return json.load(f).get("dram_bytes_per_launch")
+    except (OSError, ValueError):
+        return None
+
+
+def check_against_oracle(out, q, k, v, units, what):
+    """Compare a few (batch) rows of a step's output with the CPU oracle."""
+    import numpy as np
+    from oracle import kv_oracle as O
+    for b in units:
+        ref = O.decode_attention(q[b:b + 1].cpu().numpy(), k[b:b + 1].cpu().numpy(),
+                                 v[b:b + 1].cpu().numpy(), SCALE)
+        got = out[b:b + 1].float().cpu().numpy()
+        err = np.abs(got - ref)
+        if not (err <= 2e-3 + 1e-2 * np.abs(ref)).all():
+            raise SystemExit(f"bench: {what} output mismatch vs oracle (max err {err.max():.3e})")
+
+
+def e2e_host_buffers(torch, L, dev, steps):
+    """Config-1 fp16 step through the public op with pinned host inputs:
+    H2D q, k, v + decode + D2H out inside the timed region."""
+    b, s = C1["batch"], C1["seqlen"]
+    g = torch.Generator().manual_seed(5)
+    qh = torch.randn(b, HQ, D, generator=g).half().pin_memory()
+    kh = torch.randn(b, HKV, s, D, generator=g).half().pin_memory()
+    vh = torch.randn(b, HKV, s, D, generator=g).half().pin_memory()
+    oh = torch.empty(b, HQ, D, dtype=torch.float16).pin_memory()
+    qd, kd, vd = (torch.empty_like(x, device=dev) for x in (qh, kh, vh))
+
+    def step():
+        qd.copy_(qh, non_blocking=True)
+        kd.copy_(kh, non_blocking=True)
+        vd.copy_(vh, non_blocking=True)
+        out = L.decode_attention(qd, kd, vd, SCALE)
+        oh.copy_(out, non_blocking=True)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    h2d = (qh.numel() + kh.numel() + vh.numel()) * 2
+    return ms, h2d, oh.numel() * 2
+
+
+def e2e_decode_step(torch, L, dev, steps):
+    """A serving-style decode step at config 1: the fp16 cache stays resident
+    in a preallocated [B, Hkv, S_max, D] buffer; each step uploads q and the new
+    token's K/V from pinned memory, writes them in place, attends over the live
+    length and reads the output back."""
+    b, s = C1["batch"], C1["seqlen"]
+    buf = s + steps + 8
+    g = torch.Generator(device=dev).manual_seed(6)
+    kc = torch.randn(b, HKV, buf, D, generator=g, device=dev).half()
+    vc = torch.randn(b, HKV, buf, D, generator=g, device=dev).half()
+    qh = torch.randn(b, HQ, D).half().pin_memory()
+    nk = torch.randn(b, HKV, 1, D).half().pin_memory()
+    nv = torch.randn(b, HKV, 1, D).half().pin_memory()
+    oh = torch.empty(b, HQ, D, dtype=torch.float16).pin_memory()
+    qd = torch.empty(b, HQ, D, dtype=torch.float16, device=dev)
+    pos = [s - 1]
+
+    def step():
+        p = pos[0]
+        qd.copy_(qh, non_blocking=True)
+        kc[:, :, p:p + 1].copy_(nk, non_blocking=True)
+        vc[:, :, p:p + 1].copy_(nv, non_blocking=True)
+        out = L.decode_attention(qd, kc, vc, SCALE, p + 1)
+        oh.copy_(out, non_blocking=True)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+        pos[0] += 1
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def run_ours(args):
+    import torch
+    world, rank, local = dist_env()
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl")
+    dev = torch.device("cuda", local if world > 1 else 0)
+    torch.cuda.set_device(dev)
+    import llmik_cuda as L
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    steps, warmup = args.steps, max(3, args.warmup)
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    sampler = ClockSampler(physical_index(local))
+    sampler.start()
+
+    # ---- config 1 per rank: fp16 (headline), INT8 (config 2), INT4 (config 3) ----
+    b, s = C1["batch"], C1["seqlen"]
+    slab0 = rank * b * HKV
+    formats = {}
+    head_ms = None
+    for fmt, name in (("f16", "fp16"), ("int8", "int8_per_token"), ("int4_asym", "int4_kivi_asym_g128"),
+                      ("int4", "int4_kivi_sym_g128")):
+        nb = algo_bytes(fmt, b, s)
+        wl = Workload(torch, L, dev, fmt, b, s, slab0, copies_for(nb, l2))
+        if fmt == "f16":
+            q, k, v = wl.sets[0]
+            check_against_oracle(wl.step(0), q, k, v, [0, b - 1], "config-1 fp16")
+        ms = max_over_ranks(torch, time_graph(torch, wl, steps, warmup, barrier), world)
+        formats[name] = {"us_per_step": ms * 1e3, "TB_s": world * nb / (ms * 1e-3) / 1e12,
+                         "bytes_per_step_per_gpu": nb, "copies_rotated": len(wl.sets)}
+        if fmt == "f16":
+            head_ms = ms
+        del wl
+        torch.cuda.empty_cache()
+    fp16_us = formats["fp16"]["us_per_step"]
+    for f in formats.values():
+        f["speedup_vs_fp16"] = fp16_us / f["us_per_step"]
+
+    # ---- config 4: batch 64, seqlen 32768 sharded by (batch, kv-head) ----
+    c4 = {}
+    if not args.no_c4 and C4["batch"] % world == 0:
+        bl = C4["batch"] // world
+        c4steps = max(1, min(steps, 100))
+        for fmt, name in (("f16", "fp16"), ("int4_asym", "int4_kivi_asym_g128")):
+            nb = algo_bytes(fmt, bl, C4["seqlen"])
+            wl = Workload(torch, L, dev, fmt, bl, C4["seqlen"], rank * bl * HKV, copies_for(nb, l2), seed=2000)
+            ms = max_over_ranks(torch, time_graph(torch, wl, c4steps, warmup, barrier, min_warm_s=0.5), world)
+            c4[name] = {"us_per_step": ms * 1e3, "TB_s": world * nb / (ms * 1e-3) / 1e12,
+                        "steps": c4steps, "batch_per_gpu": bl}
+            if fmt == "f16":
+                # assemble the output shards (NCCL all-gather, off the timed path)
+                # and check the last sequence against the oracle on rank 0
+                out = wl.step(0)
+                full = out
+                if dist is not None:
+                    parts = [torch.empty_like(out) for _ in range(world)]
+                    dist.all_gather(parts, out)
+                    full = torch.cat(parts)
+                if rank == 0:
+                    bl_last = C4["batch"] - 1
+                    kk, vv = make_slabs(torch, dev, 1, C4["seqlen"], bl_last * HKV, 2000, False)
+                    gq = torch.Generator(device=dev).manual_seed(2000 + 7 * 10**6 + (world - 1) * bl * HKV)
+                    qq = torch.randn(bl, HQ, D, generator=gq, device=dev).half()[-1:]
+                    check_against_oracle(full[-1:], qq, kk, vv, [0], "config-4 fp16 (gathered)")
+                    c4[name]["verified"] = "last sequence of the gathered output vs CPU oracle"
+            del wl
+            torch.cuda.empty_cache()
+    clocks = sampler.stop()
+
+    # ---- end to end through the public op (host buffers) ----
+    e2e_steps = max(3, min(steps, 20))
+    e2e_ms, h2d, d2h = e2e_host_buffers(torch, L, dev, e2e_steps)
+    e2e_ms = max_over_ranks(torch, e2e_ms, world)
+    dec_ms = max_over_ranks(torch, e2e_decode_step(torch, L, dev, max(10, min(steps, 200))), world)
+
+    nb1 = algo_bytes("f16", b, s)
+    value = world * nb1 / (head_ms * 1e-3) / 1e12
+    peak, peak_kind = measured_hbm_peak()
+    achieved = nb1 / (head_ms * 1e-3) / 1e9
+    line = {
+        "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": world, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": head_ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic: seeded N(0,1) per (batch, kv-head) slab, cast to fp16",
+        "config": {"workload": "config1: fp16 KV GQA decode, batch 8 per GPU, 32 q / 8 kv heads, "
+                               "head_dim 128, seqlen 4096",
+                   "global_batch": b * world, "seq_len": s, "n_heads": HQ, "n_kv_heads": HKV,
+                   "head_dim": D, "parallelism": f"shard(batch, kv_head) x{world}",
+                   "l2": "inputs rotated over copies totalling > 3x L2 (every step streams from HBM)"},
+        "us_per_step": head_ms * 1e3,
+        "tokens_per_s": world * b / (head_ms * 1e-3),
+        "formats": formats,
+        "config4_sharded": c4,
+        "e2e": {"value": world * nb1 / (e2e_ms * 1e-3) / 1e12, "unit": "TB/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+                "what": "llmik_cuda.decode_attention with q, k, v copied from pinned host memory "
+                        "and the output copied back, every step"},
+        "e2e_decode_step": {"us_per_step": dec_ms * 1e3,
+                            "what": "resident fp16 cache; per step H2D q + new K/V token, in-place "
+                                    "append, decode over the live length, D2H output"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": ncu_traffic(), "peak_source": peak_kind,
+                     "kernel": "decode_kernel<fp16, 4 heads/unit>"},
+        "clocks": clocks,
+        "gpu_launches": steps,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        med, _, cores = cpu_unit_sample(5, 1)
+        n = max(5, min(4000, int(15.0 / max(med, 1e-4))))
+        med, total, cores = cpu_unit_sample(n, 1)
+        line["cpu_baseline"] = {"value": unit_bytes_c1() / med / 1e12, "unit": "TB/s", "cores": cores,
+                                "kind": "port", "seconds": total,
+                                "sample": f"{n} steps x one (batch, kv-head) unit of config 1 on the CPU "
+                                          f"oracle (numpy port of reference/attention_ref.py); {cpu_info()}"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -71,6 +71,8 @@ lik_status check_heads(int64_t batch, int64_t n_heads, int64_t n_kv_heads, int64
 lik_status check_len(int64_t seqlen, int64_t kv_buf_len) {
     if (seqlen < 1) return fail(LIK_ERR_INVALID_ARGUMENT, "seqlen must be >= 1");
     if (kv_buf_len < seqlen) return fail(LIK_ERR_INVALID_ARGUMENT, "seqlen exceeds allocated cache length");
+    if (kv_buf_len > (int64_t{1} << 30))
+        return fail(LIK_ERR_INVALID_ARGUMENT, "cache length above 2^30 positions is not supported");
     return LIK_OK;
 }
 

@@ -24,15 +24,17 @@
 //   warps 0-7 (consumers): warp w owns positions [w*T/8, (w+1)*T/8) of every
 //     tile and keeps its own online-softmax state (m, l, acc) for all HB heads,
 //     so the tile loop has no CTA-wide barrier. Per warp and tile:
-//       QK : 8 lanes per position, 16 channels per lane, packed half2 FMAs on
-//            dequantized codes (the K group scale of INT4 is folded into q once
-//            per group, the INT8 token scale applied to the reduced score),
-//            partial sums reduce-scattered over the 8 lanes so each lane ends
-//            with one head's score.
+//       QK : 8 lanes per position, 16 channels per lane. K codes are
+//            dequantized to fp16 exactly as the reference oracle does
+//            (fp16(code * scale [+ zero]); the INT8 token scale multiplies
+//            the reduced score instead), then multiplied with q in fp16 by
+//            sm_100's mixed-precision fma.rn.f32.f16 (exact product, fp32
+//            sum). Partial sums are reduce-scattered over the 8 lanes so each
+//            lane ends with one head's score.
 //       softmax: scores are in the log2 domain (q pre-scaled by
 //            softmax_scale * log2 e); warp-shuffle max/sum; exp2 on MUFU.
-//       PV : lanes own output channels, fp32 accumulation; the V token scale is
-//            folded into p, the asymmetric V zero point into a per-head sum.
+//       PV : lanes own output channels; V dequantized to fp16 like K;
+//            acc += p(fp16) * v(fp16) with the same mixed-precision FMA.
 //   At a unit boundary the 8 warp states are merged in shared memory.
 //
 // Every mbarrier wait is bounded (kMaxPolls); on expiry the kernel records
@@ -58,12 +60,12 @@ template <int FMT>
 struct Fmt;
 template <>
 struct Fmt<kF16> {
-    static constexpr int ROWB = 256, T = 64, PVC = 4;
+    static constexpr int ROWB = 256, T = 128, PVC = 4;
     static constexpr bool TOKK = false, TOKV = false, ZV = false, KG = false, ZK = false, SIGNED = true;
 };
 template <>
 struct Fmt<kI8> {
-    static constexpr int ROWB = 128, T = 128, PVC = 4;
+    static constexpr int ROWB = 128, T = 256, PVC = 4;
     static constexpr bool TOKK = true, TOKV = true, ZV = false, KG = false, ZK = false, SIGNED = true;
 };
 template <>
@@ -161,6 +163,25 @@ __device__ __forceinline__ long long cta_first_tile(long long c, long long total
     return c * total / nctas;
 }
 
+// The HB fp16 softmax weights of one position (8-byte aligned for HB = 4).
+template <int HB>
+__device__ __forceinline__ void load_p(const uint16_t* src, uint16_t (&ph)[HB]) {
+    if constexpr (HB == 4) {
+        const uint2 u = *reinterpret_cast<const uint2*>(src);
+        ph[0] = u.x & 0xffff; ph[1] = u.x >> 16; ph[2] = u.y & 0xffff; ph[3] = u.y >> 16;
+    } else if constexpr (HB == 8) {
+        const uint4 u = *reinterpret_cast<const uint4*>(src);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) { ph[2 * i] = w[i] & 0xffff; ph[2 * i + 1] = w[i] >> 16; }
+    } else if constexpr (HB == 2) {
+        const uint32_t u = *reinterpret_cast<const uint32_t*>(src);
+        ph[0] = u & 0xffff; ph[1] = u >> 16;
+    } else {
+        ph[0] = src[0];
+    }
+}
+
 __device__ __forceinline__ float h2_sum(half2 a) {
     const float2 f = __half22float2(a);
     return f.x + f.y;
@@ -206,10 +227,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
         const uint64_t pol = l2_policy_evict_first();
         long long j = 0;
         bool ok = true;
+        // incremental (stage, phase) and (unit, tile) counters: no divisions in the loop
+        int st = 0;
+        uint32_t ph = 0;
+        long long unit = tb / p.tpu;
+        long long ti = tb - unit * p.tpu;
+        long long bk = unit / p.nhb;
         for (long long i = tb; i < te; ++i, ++j) {
-            const int st = static_cast<int>(j % p.nst);
             if (j >= p.nst) {
-                const uint32_t par = static_cast<uint32_t>(((j / p.nst) - 1) & 1);
+                const uint32_t par = ph ^ 1u;
                 bool got = false;
                 for (uint32_t it = 0; it < kMaxPolls; ++it) {
                     if (mbar_try_wait(&empty[st], par)) {
@@ -223,11 +249,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                     break;
                 }
             }
-            const long long unit = i / p.tpu;
-            const long long ti = i - unit * p.tpu;
             const long long t0 = ti * T;
             const int ntok = static_cast<int>(min(static_cast<long long>(T), p.seqlen - t0));
-            const long long bk = unit / p.nhb;
             const long long rowbase = bk * p.kv_buf_len + t0;
             uint8_t* sb = smem + static_cast<size_t>(st) * p.stage_bytes;
             const int n8 = (ntok + 7) & ~7;
@@ -247,8 +270,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                     bytes += (F::TOKK + F::TOKV + F::ZV) * n8 * 2;
                 }
                 if (F::KG && p.kg_smem) {
-                    g0 = static_cast<int>(t0 / p.group_size);
-                    const int g1 = static_cast<int>((t0 + ntok - 1) / p.group_size);
+                    g0 = static_cast<int>(t0) / p.group_size;
+                    const int g1 = (static_cast<int>(t0) + ntok - 1) / p.group_size;
                     ngrp = g1 - g0 + 1;
                     bytes += (F::ZK ? 2 : 1) * ngrp * kHeadDim * 2;
                 }
@@ -267,6 +290,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                 }
             } else {
                 mbar_arrive(&full[st]);
+            }
+            if (++st == p.nst) {
+                st = 0;
+                ph ^= 1u;
+            }
+            if (++ti == p.tpu) {
+                ti = 0;
+                ++unit;
+                bk = unit / p.nhb;
             }
         }
         if (!ok) {
@@ -288,30 +320,27 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
     const bool prim = head_primary<HB>(lane);
     const int nct = kNCW * 32;
 
-    float* pbuf = reinterpret_cast<float*>(smem + p.off_work) + w * TW * HB;
+    uint16_t* pbuf = reinterpret_cast<uint16_t*>(smem + p.off_work) + w * TW * HB;  // p as f16
     float* abuf = reinterpret_cast<float*>(smem + p.off_work);
     float* mlb = reinterpret_cast<float*>(smem + p.off_ml);
 
-    float m_run = -INFINITY, l_run = 0.f, z_run = 0.f;
+    float m_run = -INFINITY, l_run = 0.f;
     float acc[HB][PVC];
     uint32_t qh[HB][8];  // q * softmax_scale * log2e as half2, in the format's pair order
-    uint32_t qs[HB][8];  // INT4: qh * k group scale
-    float qb[HB];        // INT4 asym: sum over the lane's channels of qh * k group zero
+    uint32_t kg[8];      // INT4: K group scale of the lane's 16 channels (pair order)
+    uint32_t kgz[8];     // INT4 asym: K group zero
     long long cur_unit = -1, seg_t0 = 0, qoff = 0, bk = 0;
     int cur_g = -1;
+    int gnext = 0;  // INT4: first position (within the unit) of the next K group
     bool aborted = false;
-
 #pragma unroll
-    for (int h = 0; h < HB; ++h) {
-        qb[h] = 0.f;
-#pragma unroll
-        for (int c = 0; c < 8; ++c) qs[h][c] = 0u;
-    }
+    for (int c = 0; c < 8; ++c) kg[c] = kgz[c] = 0u;
 
-    long long j = 0;
-    for (long long i = tb; i < te; ++i, ++j) {
-        const long long unit = i / p.tpu;
-        const long long ti = i - unit * p.tpu;
+    int st = 0;
+    uint32_t ph = 0;
+    long long unit = tb / p.tpu;
+    long long ti = tb - unit * p.tpu;
+    for (long long i = tb; i < te; ++i) {
         if (unit != cur_unit) {
             // ---- start of a unit segment: load q for the HB heads ----
             cur_unit = unit;
@@ -324,7 +353,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
             qoff = (b * p.n_heads + static_cast<long long>(kvh) * p.nhb * HB + hb * HB) * kHeadDim;
             m_run = -INFINITY;
             l_run = 0.f;
-            z_run = 0.f;
 #pragma unroll
             for (int h = 0; h < HB; ++h) {
 #pragma unroll
@@ -361,9 +389,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
             }
         }
 
-        const int st = static_cast<int>(j % p.nst);
         if (!aborted) {
-            if (misc[0] || !mbar_wait_bounded(&full[st], static_cast<uint32_t>((j / p.nst) & 1))) {
+            if (misc[0] || !mbar_wait_bounded(&full[st], ph)) {
                 aborted = true;
                 misc[0] = 1;
                 if (lane == 0) atomicExch(p.err, kDevWaitTimeout);
@@ -384,89 +411,66 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
             const int nval = min(TW, ntok - wt0);
 
             // ---------------- QK ----------------
+            // K is dequantized to fp16 with the oracle's rounding (fp16(code *
+            // scale [+ zero])); products f16 x f16 are exact, sums in fp32.
             float sc[NP];
 #pragma unroll
             for (int pp = 0; pp < NP; ++pp) {
                 const int tt = wt0 + pp * 4 + grp;
                 float part[HB];
+#pragma unroll
+                for (int h = 0; h < HB; ++h) part[h] = 0.f;
                 if (tt < ntok) {
                     const uint8_t* row = sK + tt * ROWB;
+                    uint32_t kk[8];
                     if (FMT == kF16) {
                         const uint4 ka = *reinterpret_cast<const uint4*>(row + jl * 16);
                         const uint4 kb = *reinterpret_cast<const uint4*>(row + 128 + jl * 16);
-                        const uint32_t kk[8] = {ka.x, ka.y, ka.z, ka.w, kb.x, kb.y, kb.z, kb.w};
-#pragma unroll
-                        for (int h = 0; h < HB; ++h) {
-                            half2 a = __hmul2(as_h2(qh[h][0]), as_h2(kk[0]));
-#pragma unroll
-                            for (int c = 1; c < 8; ++c) a = __hfma2(as_h2(qh[h][c]), as_h2(kk[c]), a);
-                            part[h] = h2_sum(a);
-                        }
+                        kk[0] = ka.x; kk[1] = ka.y; kk[2] = ka.z; kk[3] = ka.w;
+                        kk[4] = kb.x; kk[5] = kb.y; kk[6] = kb.z; kk[7] = kb.w;
                     } else if (FMT == kI8) {
+                        // raw codes; the token scale multiplies the reduced score
                         const uint4 ka = *reinterpret_cast<const uint4*>(row + jl * 16);
-                        half2 kk[8];
-                        i8x4_to_h2(ka.x, kk[0], kk[1]);
-                        i8x4_to_h2(ka.y, kk[2], kk[3]);
-                        i8x4_to_h2(ka.z, kk[4], kk[5]);
-                        i8x4_to_h2(ka.w, kk[6], kk[7]);
-#pragma unroll
-                        for (int h = 0; h < HB; ++h) {
-                            half2 a = __hmul2(as_h2(qh[h][0]), kk[0]);
-#pragma unroll
-                            for (int c = 1; c < 8; ++c) a = __hfma2(as_h2(qh[h][c]), kk[c], a);
-                            part[h] = h2_sum(a);
-                        }
+                        half2 a0, a1;
+                        i8x4_to_h2(ka.x, a0, a1); kk[0] = as_u32(a0); kk[1] = as_u32(a1);
+                        i8x4_to_h2(ka.y, a0, a1); kk[2] = as_u32(a0); kk[3] = as_u32(a1);
+                        i8x4_to_h2(ka.z, a0, a1); kk[4] = as_u32(a0); kk[5] = as_u32(a1);
+                        i8x4_to_h2(ka.w, a0, a1); kk[6] = as_u32(a0); kk[7] = as_u32(a1);
                     } else {
-                        // INT4: fold the K group scale (and zero) into q on group change
-                        const int g = static_cast<int>((t0 + tt) / p.group_size);
-                        if (g != cur_g) {
+                        const int tabs = static_cast<int>(t0) + tt;
+                        if (cur_g < 0 || tabs >= gnext) {
+                            const int g = tabs / p.group_size;
                             cur_g = g;
-                            const __half* gs;
-                            const __half* gz = nullptr;
+                            gnext = (g + 1) * p.group_size;
+                            const __half* gsp;
+                            const __half* gzp = nullptr;
                             if (p.kg_smem) {
-                                const int g0 = static_cast<int>(t0 / p.group_size);
-                                gs = reinterpret_cast<const __half*>(sb + p.off_kgs) + (g - g0) * kHeadDim;
-                                if (F::ZK) gz = reinterpret_cast<const __half*>(sb + p.off_kgz) + (g - g0) * kHeadDim;
+                                const int g0 = static_cast<int>(t0) / p.group_size;
+                                gsp = reinterpret_cast<const __half*>(sb + p.off_kgs) + (g - g0) * kHeadDim;
+                                if (F::ZK) gzp = reinterpret_cast<const __half*>(sb + p.off_kgz) + (g - g0) * kHeadDim;
                             } else {
                                 const long long gb = (bk * p.ng_buf + g) * kHeadDim;
-                                gs = p.ks + gb;
-                                if (F::ZK) gz = p.kz + gb;
+                                gsp = p.ks + gb;
+                                if (F::ZK) gzp = p.kz + gb;
                             }
-                            const uint4 s0 = *reinterpret_cast<const uint4*>(gs + 16 * jl);
-                            const uint4 s1 = *reinterpret_cast<const uint4*>(gs + 16 * jl + 8);
+                            const uint4 s0 = *reinterpret_cast<const uint4*>(gsp + 16 * jl);
+                            const uint4 s1 = *reinterpret_cast<const uint4*>(gsp + 16 * jl + 8);
                             const __half* sh0 = reinterpret_cast<const __half*>(&s0);
                             const __half* sh1 = reinterpret_cast<const __half*>(&s1);
-                            half2 sp[8];
 #pragma unroll
                             for (int k = 0; k < 4; ++k) {
-                                sp[k] = __halves2half2(sh0[k], sh0[k + 4]);
-                                sp[4 + k] = __halves2half2(sh1[k], sh1[k + 4]);
+                                kg[k] = as_u32(__halves2half2(sh0[k], sh0[k + 4]));
+                                kg[4 + k] = as_u32(__halves2half2(sh1[k], sh1[k + 4]));
                             }
-#pragma unroll
-                            for (int h = 0; h < HB; ++h)
-#pragma unroll
-                                for (int c = 0; c < 8; ++c) qs[h][c] = as_u32(__hmul2(as_h2(qh[h][c]), sp[c]));
                             if (F::ZK) {
-                                const uint4 z0 = *reinterpret_cast<const uint4*>(gz + 16 * jl);
-                                const uint4 z1 = *reinterpret_cast<const uint4*>(gz + 16 * jl + 8);
+                                const uint4 z0 = *reinterpret_cast<const uint4*>(gzp + 16 * jl);
+                                const uint4 z1 = *reinterpret_cast<const uint4*>(gzp + 16 * jl + 8);
                                 const __half* zh0 = reinterpret_cast<const __half*>(&z0);
                                 const __half* zh1 = reinterpret_cast<const __half*>(&z1);
-                                half2 zp[8];
 #pragma unroll
                                 for (int k = 0; k < 4; ++k) {
-                                    zp[k] = __halves2half2(zh0[k], zh0[k + 4]);
-                                    zp[4 + k] = __halves2half2(zh1[k], zh1[k + 4]);
-                                }
-#pragma unroll
-                                for (int h = 0; h < HB; ++h) {
-                                    float s = 0.f;
-#pragma unroll
-                                    for (int c = 0; c < 8; ++c) {
-                                        const float2 a = __half22float2(as_h2(qh[h][c]));
-                                        const float2 z = __half22float2(zp[c]);
-                                        s = fmaf(a.x, z.x, fmaf(a.y, z.y, s));
-                                    }
-                                    qb[h] = s;
+                                    kgz[k] = as_u32(__halves2half2(zh0[k], zh0[k + 4]));
+                                    kgz[4 + k] = as_u32(__halves2half2(zh1[k], zh1[k + 4]));
                                 }
                             }
                         }
@@ -475,18 +479,25 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                         i4x8_to_h2<F::SIGNED>(kw.x, c0);
                         i4x8_to_h2<F::SIGNED>(kw.y, c1);
 #pragma unroll
-                        for (int h = 0; h < HB; ++h) {
-                            half2 a = __hmul2(as_h2(qs[h][0]), c0[0]);
-#pragma unroll
-                            for (int c = 1; c < 4; ++c) a = __hfma2(as_h2(qs[h][c]), c0[c], a);
-#pragma unroll
-                            for (int c = 0; c < 4; ++c) a = __hfma2(as_h2(qs[h][4 + c]), c1[c], a);
-                            part[h] = h2_sum(a) + (F::ZK ? qb[h] : 0.f);
+                        for (int k = 0; k < 4; ++k) {
+                            if (F::ZK) {
+                                kk[k] = as_u32(__hfma2(c0[k], as_h2(kg[k]), as_h2(kgz[k])));
+                                kk[4 + k] = as_u32(__hfma2(c1[k], as_h2(kg[4 + k]), as_h2(kgz[4 + k])));
+                            } else {
+                                kk[k] = as_u32(__hmul2(c0[k], as_h2(kg[k])));
+                                kk[4 + k] = as_u32(__hmul2(c1[k], as_h2(kg[4 + k])));
+                            }
                         }
                     }
-                } else {
+                    float part2[HB];
 #pragma unroll
-                    for (int h = 0; h < HB; ++h) part[h] = 0.f;
+                    for (int h = 0; h < HB; ++h) part2[h] = 0.f;
+#pragma unroll
+                    for (int c = 0; c < 8; ++c)
+#pragma unroll
+                        for (int h = 0; h < HB; ++h) fma_h2_2acc(qh[h][c], kk[c], part[h], part2[h]);
+#pragma unroll
+                    for (int h = 0; h < HB; ++h) part[h] += part2[h];
                 }
                 float s = reduce_scatter8<HB>(part, lane);
                 if (tt >= ntok) {
@@ -505,27 +516,17 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
             mloc = fmaxf(mloc, __shfl_xor_sync(kFull, mloc, 16));
             const float mnew = fmaxf(m_run, mloc);
             const float alpha = fast_exp2(m_run - mnew);
-            float ls = 0.f, zs = 0.f;
+            float ls = 0.f;
 #pragma unroll
             for (int pp = 0; pp < NP; ++pp) {
                 const int tl = pp * 4 + grp;  // position within the warp's share
                 const float e = fast_exp2(sc[pp] - mnew);
                 ls += e;
-                if (tl < nval) {
-                    float pv = e;
-                    if (F::TOKV) pv *= __half2float(svs[wt0 + tl]);
-                    if (F::ZV) zs = fmaf(e, __half2float(svz[wt0 + tl]), zs);
-                    if (prim) pbuf[tl * HB + hh] = pv;
-                }
+                if (tl < nval && prim) pbuf[tl * HB + hh] = __half_as_ushort(__float2half_rn(e));
             }
             ls += __shfl_xor_sync(kFull, ls, 8);
             ls += __shfl_xor_sync(kFull, ls, 16);
-            if (F::ZV) {
-                zs += __shfl_xor_sync(kFull, zs, 8);
-                zs += __shfl_xor_sync(kFull, zs, 16);
-            }
             l_run = fmaf(l_run, alpha, ls);
-            z_run = fmaf(z_run, alpha, zs);
             m_run = mnew;
             float al[HB];
 #pragma unroll
@@ -537,29 +538,35 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                 for (int c = 0; c < PVC; ++c) acc[h][c] *= al[h];
 
             // ---------------- PV ----------------
+            // V dequantized to fp16 as the oracle does; acc += p(f16) * v(f16) in fp32.
             if (FMT == kF16 || FMT == kI8) {
-                for (int t = 0; t < nval; ++t) {
-                    float vf[4];
+                auto pv_token = [&](int t) {
+                    uint32_t v0, v1;
                     if (FMT == kF16) {
                         const uint2 vv = *reinterpret_cast<const uint2*>(sV + (wt0 + t) * ROWB + lane * 8);
-                        const float2 a = __half22float2(as_h2(vv.x));
-                        const float2 b = __half22float2(as_h2(vv.y));
-                        vf[0] = a.x; vf[1] = a.y; vf[2] = b.x; vf[3] = b.y;
+                        v0 = vv.x;
+                        v1 = vv.y;
                     } else {
                         const uint32_t vv = *reinterpret_cast<const uint32_t*>(sV + (wt0 + t) * ROWB + lane * 4);
                         half2 lo, hi;
                         i8x4_to_h2(vv, lo, hi);
-                        const float2 a = __half22float2(lo);
-                        const float2 b = __half22float2(hi);
-                        vf[0] = a.x; vf[1] = a.y; vf[2] = b.x; vf[3] = b.y;
+                        const half2 s2 = __half2half2(svs[wt0 + t]);
+                        v0 = as_u32(__hmul2(lo, s2));
+                        v1 = as_u32(__hmul2(hi, s2));
                     }
-                    const float* pr = pbuf + t * HB;
+                    uint16_t ph[HB];
+                    load_p<HB>(pbuf + t * HB, ph);
 #pragma unroll
                     for (int h = 0; h < HB; ++h) {
-                        const float ph = pr[h];
-#pragma unroll
-                        for (int c = 0; c < 4; ++c) acc[h][c] = fmaf(ph, vf[c], acc[h][c]);
+                        fma_s_h2(ph[h], v0, acc[h][0], acc[h][1]);
+                        fma_s_h2(ph[h], v1, acc[h][2], acc[h][3]);
                     }
+                };
+                if (nval == TW) {
+#pragma unroll 4
+                    for (int t = 0; t < TW; ++t) pv_token(t);
+                } else {
+                    for (int t = 0; t < nval; ++t) pv_token(t);
                 }
             } else {
                 const int hw = lane >> 4;
@@ -568,20 +575,22 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                     const uint32_t vv = *reinterpret_cast<const uint32_t*>(sV + (wt0 + t) * ROWB + l16 * 4);
                     half2 o[4];
                     i4x8_to_h2<F::SIGNED>(vv, o);
-                    float vf[8];
+                    const half2 s2 = __half2half2(svs[wt0 + t]);
+                    uint32_t vd[4];
+                    if (F::ZV) {
+                        const half2 z2 = __half2half2(svz[wt0 + t]);
 #pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        const float2 f = __half22float2(o[k]);
-                        vf[2 * k] = f.x;
-                        vf[2 * k + 1] = f.y;
+                        for (int k = 0; k < 4; ++k) vd[k] = as_u32(__hfma2(o[k], s2, z2));
+                    } else {
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) vd[k] = as_u32(__hmul2(o[k], s2));
                     }
-                    const float* pr = pbuf + t * HB;
+                    uint16_t ph[HB];
+                    load_p<HB>(pbuf + t * HB, ph);
 #pragma unroll
-                    for (int h = 0; h < HB; ++h) {
-                        const float ph = pr[h];
+                    for (int h = 0; h < HB; ++h)
 #pragma unroll
-                        for (int c = 0; c < 8; ++c) acc[h][c] = fmaf(ph, vf[c], acc[h][c]);
-                    }
+                        for (int k = 0; k < 4; ++k) fma_s_h2(ph[h], vd[k], acc[h][2 * k], acc[h][2 * k + 1]);
                 }
             }
             __syncwarp();
@@ -601,7 +610,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                 float* e = mlb + (w * HB + hh) * 3;
                 e[0] = m_run;
                 e[1] = l_run;
-                e[2] = z_run;
             }
             named_bar_sync(1, nct);
 #pragma unroll
@@ -629,15 +637,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                 const int h = o >> 7;
                 float M = -INFINITY;
                 for (int ww = 0; ww < kNCW; ++ww) M = fmaxf(M, mlb[(ww * HB + h) * 3]);
-                float L = 0.f, Z = 0.f, A = 0.f;
+                float L = 0.f, A = 0.f;
                 for (int ww = 0; ww < kNCW; ++ww) {
                     const float* e = mlb + (ww * HB + h) * 3;
-                    const float f = fast_exp2(e[0] - M);
-                    L = fmaf(e[1], f, L);
-                    if (F::ZV) Z = fmaf(e[2], f, Z);
+                    L = fmaf(e[1], fast_exp2(e[0] - M), L);
                     A += abuf[(ww * HB + h) * kHeadDim + (o & 127)];
                 }
-                A += Z;
                 if (whole) {
                     p.out[qoff + o] = __float2half_rn(A / L);
                 } else {
@@ -686,6 +691,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
             }
             named_bar_sync(1, nct);
         }
+        if (++st == p.nst) {
+            st = 0;
+            ph ^= 1u;
+        }
+        if (++ti == p.tpu) {
+            ti = 0;
+            ++unit;
+        }
     }
 }
 
@@ -701,18 +714,19 @@ int heads_per_unit(int64_t group, int fmt) {
     return 1;
 }
 
+// Workspace layout (bytes): [error word | partial slots | unit counters].
+// The partial-slot region has a fixed capacity (two slots per SM at the
+// largest slot stride), so the counters always start at the same offset:
+// calls with different shapes sharing one workspace never find a counter on
+// top of another call's partial results. Counters are left zero by every call.
+static size_t partial_region_bytes(int sm_count) {
+    return align_up(static_cast<size_t>(2) * sm_count * (8 * kHeadDim + 2 * 8) * 4, 256);
+}
+
 size_t decode_workspace_bytes(int64_t batch, int64_t n_heads, int64_t n_kv_heads, int sm_count) {
     if (batch <= 0 || n_kv_heads <= 0 || n_heads <= 0) return kWsErrBytes;
-    const int64_t g = n_heads / n_kv_heads;
-    size_t best = 0;
-    for (int fmt = kF16; fmt <= kI4Asym; ++fmt) {
-        const int hb = heads_per_unit(g, fmt);
-        const int64_t n_units = batch * n_kv_heads * (g / hb);
-        const size_t counters = align_up(static_cast<size_t>(n_units) * 4, 256);
-        const size_t slots = static_cast<size_t>(2) * sm_count * (hb * kHeadDim + 2 * hb) * 4;
-        best = std::max(best, kWsErrBytes + counters + slots);
-    }
-    return best;
+    const int64_t n_units = batch * n_heads;  // upper bound over every heads-per-unit choice
+    return kWsErrBytes + partial_region_bytes(sm_count) + align_up(static_cast<size_t>(n_units) * 4, 256);
 }
 
 namespace {
@@ -799,10 +813,10 @@ lik_status launch_t(const DecodeArgs& a, const DeviceInfo& di, cudaStream_t stre
 
     uint8_t* ws = static_cast<uint8_t*>(a.workspace);
     p.err = reinterpret_cast<int*>(ws);
-    p.counters = reinterpret_cast<unsigned*>(ws + kWsErrBytes);
-    p.part = reinterpret_cast<float*>(ws + kWsErrBytes + align_up(static_cast<size_t>(p.n_units) * 4, 256));
-    const size_t need = kWsErrBytes + align_up(static_cast<size_t>(p.n_units) * 4, 256) +
-                        static_cast<size_t>(2) * p.n_ctas * (HB * kHeadDim + 2 * HB) * 4;
+    p.part = reinterpret_cast<float*>(ws + kWsErrBytes);
+    p.counters = reinterpret_cast<unsigned*>(ws + kWsErrBytes + partial_region_bytes(di.sm_count));
+    const size_t need = kWsErrBytes + partial_region_bytes(di.sm_count) +
+                        align_up(static_cast<size_t>(p.n_units) * 4, 256);
     if (a.workspace == nullptr || a.workspace_bytes < need) {
         err = "workspace too small: need " + std::to_string(need) + " bytes";
         return LIK_ERR_WORKSPACE;

@@ -147,3 +147,47 @@ __device__ __forceinline__ void i4x8_to_h2(uint32_t w, half2 (&o)[4]) {
 }
 
 }  // namespace lik
+
+namespace lik {
+
+// ---- mixed-precision FMA (sm_100): d = a(f16) * b(f16) + c(f32) ----------
+// The f16 x f16 product is exact in f32, so only the f32 accumulation rounds.
+
+// acc += a.lo * b.lo + a.hi * b.hi   (a, b: packed half2)
+__device__ __forceinline__ float fma_h2_dot(uint32_t a, uint32_t b, float acc) {
+    asm("{\n\t.reg .f16 al, ah, bl, bh;\n\t"
+        "mov.b32 {al, ah}, %1;\n\t"
+        "mov.b32 {bl, bh}, %2;\n\t"
+        "fma.rn.f32.f16 %0, al, bl, %0;\n\t"
+        "fma.rn.f32.f16 %0, ah, bh, %0;\n\t}"
+        : "+f"(acc)
+        : "r"(a), "r"(b));
+    return acc;
+}
+
+// (lo, hi) += s * (b.lo, b.hi)   (s: one f16 in the low half of a register)
+__device__ __forceinline__ void fma_s_h2(uint16_t s, uint32_t b, float& lo, float& hi) {
+    asm("{\n\t.reg .f16 bl, bh;\n\t"
+        "mov.b32 {bl, bh}, %3;\n\t"
+        "fma.rn.f32.f16 %0, %2, bl, %0;\n\t"
+        "fma.rn.f32.f16 %1, %2, bh, %1;\n\t}"
+        : "+f"(lo), "+f"(hi)
+        : "h"(s), "r"(b));
+}
+
+}  // namespace lik
+
+namespace lik {
+
+// lo += a.lo * b.lo ; hi += a.hi * b.hi   (two independent accumulation chains)
+__device__ __forceinline__ void fma_h2_2acc(uint32_t a, uint32_t b, float& lo, float& hi) {
+    asm("{\n\t.reg .f16 al, ah, bl, bh;\n\t"
+        "mov.b32 {al, ah}, %2;\n\t"
+        "mov.b32 {bl, bh}, %3;\n\t"
+        "fma.rn.f32.f16 %0, al, bl, %0;\n\t"
+        "fma.rn.f32.f16 %1, ah, bh, %1;\n\t}"
+        : "+f"(lo), "+f"(hi)
+        : "r"(a), "r"(b));
+}
+
+}  // namespace lik

@@ -216,3 +216,12 @@ def test_cabi_direct_decode_and_workspace_check(L):
     with pytest.raises(cabi.LikError, match="WORKSPACE"):
         cabi.call("lik_decode_attention_f16", qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), out.data_ptr(),
                   2, 32, 8, 128, 777, 777, SCALE, ws.data_ptr(), 300, stream)
+
+
+def test_workspace_shared_across_shapes(L):
+    """A shared workspace used first by a small call (whose partial results
+    stay behind) and then by a call with more units must give correct results."""
+    for b, s in ((1, 512), (2, 4096), (9, 2048), (1, 700), (12, 1500)):
+        q, k, v = _inputs(b, 32, 8, s, seed=b * 1000 + s)
+        out = L.decode_attention(q.cuda(), k.cuda(), v.cuda(), SCALE)
+        assert_attn_close(out.cpu().numpy(), O.decode_attention(q.numpy(), k.numpy(), v.numpy(), SCALE))
