@@ -163,23 +163,35 @@ __device__ __forceinline__ long long cta_first_tile(long long c, long long total
     return c * total / nctas;
 }
 
-// The HB fp16 softmax weights of one position (8-byte aligned for HB = 4).
+// The HB fp16 softmax weights of one position as (HB+1)/2 packed words.
 template <int HB>
-__device__ __forceinline__ void load_p(const uint16_t* src, uint16_t (&ph)[HB]) {
-    if constexpr (HB == 4) {
-        const uint2 u = *reinterpret_cast<const uint2*>(src);
-        ph[0] = u.x & 0xffff; ph[1] = u.x >> 16; ph[2] = u.y & 0xffff; ph[3] = u.y >> 16;
-    } else if constexpr (HB == 8) {
+__device__ __forceinline__ void load_pw(const uint16_t* src, uint32_t (&pw)[(HB + 1) / 2]) {
+    if constexpr (HB == 8) {
         const uint4 u = *reinterpret_cast<const uint4*>(src);
-        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) { ph[2 * i] = w[i] & 0xffff; ph[2 * i + 1] = w[i] >> 16; }
+        pw[0] = u.x; pw[1] = u.y; pw[2] = u.z; pw[3] = u.w;
+    } else if constexpr (HB == 4) {
+        const uint2 u = *reinterpret_cast<const uint2*>(src);
+        pw[0] = u.x; pw[1] = u.y;
     } else if constexpr (HB == 2) {
-        const uint32_t u = *reinterpret_cast<const uint32_t*>(src);
-        ph[0] = u & 0xffff; ph[1] = u >> 16;
+        pw[0] = *reinterpret_cast<const uint32_t*>(src);
     } else {
-        ph[0] = src[0];
+        pw[0] = src[0];
     }
+}
+
+// acc[h][2i], acc[h][2i+1] += p_h * v[i] for every head h
+template <int HB, int NV, int PVC>
+__device__ __forceinline__ void pv_accum(const uint32_t (&pw)[(HB + 1) / 2], const uint32_t (&v)[NV],
+                                         float (&acc)[HB][PVC]) {
+#pragma unroll
+    for (int h = 0; h < HB; ++h)
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            if (h & 1)
+                fma_p_h2<1>(pw[h >> 1], v[i], acc[h][2 * i], acc[h][2 * i + 1]);
+            else
+                fma_p_h2<0>(pw[h >> 1], v[i], acc[h][2 * i], acc[h][2 * i + 1]);
+        }
 }
 
 __device__ __forceinline__ float h2_sum(half2 a) {
@@ -554,13 +566,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                         v0 = as_u32(__hmul2(lo, s2));
                         v1 = as_u32(__hmul2(hi, s2));
                     }
-                    uint16_t ph[HB];
-                    load_p<HB>(pbuf + t * HB, ph);
-#pragma unroll
-                    for (int h = 0; h < HB; ++h) {
-                        fma_s_h2(ph[h], v0, acc[h][0], acc[h][1]);
-                        fma_s_h2(ph[h], v1, acc[h][2], acc[h][3]);
-                    }
+                    uint32_t pw[(HB + 1) / 2];
+                    load_pw<HB>(pbuf + t * HB, pw);
+                    const uint32_t vv2[2] = {v0, v1};
+                    pv_accum<HB, 2, PVC>(pw, vv2, acc);
                 };
                 if (nval == TW) {
 #pragma unroll 4
@@ -571,7 +580,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
             } else {
                 const int hw = lane >> 4;
                 const int l16 = lane & 15;
-                for (int t = hw; t < nval; t += 2) {
+                auto pv_token = [&](int t) {
                     const uint32_t vv = *reinterpret_cast<const uint32_t*>(sV + (wt0 + t) * ROWB + l16 * 4);
                     half2 o[4];
                     i4x8_to_h2<F::SIGNED>(vv, o);
@@ -585,12 +594,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
 #pragma unroll
                         for (int k = 0; k < 4; ++k) vd[k] = as_u32(__hmul2(o[k], s2));
                     }
-                    uint16_t ph[HB];
-                    load_p<HB>(pbuf + t * HB, ph);
-#pragma unroll
-                    for (int h = 0; h < HB; ++h)
-#pragma unroll
-                        for (int k = 0; k < 4; ++k) fma_s_h2(ph[h], vd[k], acc[h][2 * k], acc[h][2 * k + 1]);
+                    uint32_t pw[(HB + 1) / 2];
+                    load_pw<HB>(pbuf + t * HB, pw);
+                    pv_accum<HB, 4, PVC>(pw, vd, acc);
+                };
+                if (nval == TW) {
+#pragma unroll 4
+                    for (int t2 = 0; t2 < TW; t2 += 2) pv_token(t2 + hw);
+                } else {
+                    for (int t = hw; t < nval; t += 2) pv_token(t);
                 }
             }
             __syncwarp();

@@ -191,3 +191,30 @@ __device__ __forceinline__ void fma_h2_2acc(uint32_t a, uint32_t b, float& lo, f
 }
 
 }  // namespace lik
+
+namespace lik {
+
+// (lo, hi) += p * (v.lo, v.hi), p = half SEL (0: low, 1: high) of the packed
+// register pp. The half is selected inside the asm, so no extraction op.
+template <int SEL>
+__device__ __forceinline__ void fma_p_h2(uint32_t pp, uint32_t v, float& lo, float& hi) {
+    if (SEL == 0) {
+        asm("{\n\t.reg .f16 p0, p1, vl, vh;\n\t"
+            "mov.b32 {p0, p1}, %2;\n\t"
+            "mov.b32 {vl, vh}, %3;\n\t"
+            "fma.rn.f32.f16 %0, p0, vl, %0;\n\t"
+            "fma.rn.f32.f16 %1, p0, vh, %1;\n\t}"
+            : "+f"(lo), "+f"(hi)
+            : "r"(pp), "r"(v));
+    } else {
+        asm("{\n\t.reg .f16 p0, p1, vl, vh;\n\t"
+            "mov.b32 {p0, p1}, %2;\n\t"
+            "mov.b32 {vl, vh}, %3;\n\t"
+            "fma.rn.f32.f16 %0, p1, vl, %0;\n\t"
+            "fma.rn.f32.f16 %1, p1, vh, %1;\n\t}"
+            : "+f"(lo), "+f"(hi)
+            : "r"(pp), "r"(v));
+    }
+}
+
+}  // namespace lik
