@@ -89,6 +89,24 @@ lik_status lik_decode_attention_f16(
     int64_t seqlen, int64_t kv_buf_len, float softmax_scale,
     void* workspace, size_t workspace_bytes, void* stream);
 
+/* fp16 KV decode that allocates nothing and takes no workspace: for callers
+ * that cannot call cudaMalloc when they launch attention (a runtime whose
+ * device memory is already carved into its own pool, or a binding that only
+ * holds the raw pointers it was given). No counterpart in the reference.
+ * Same arguments and results as lik_decode_attention_f16 minus the
+ * workspace. Its scratch is a fixed 4 MiB array inside the library that every
+ * GPU loading the library keeps until exit; shapes whose
+ * lik_decode_workspace_bytes() exceeds 4 MiB are rejected with
+ * LIK_ERR_WORKSPACE. The first call on each device looks up that array's
+ * device address and zeroes it (synchronously), so make that first call
+ * before any stream capture. All calls on a device share the one array:
+ * calls that can overlap on the GPU (other streams, other host threads) race
+ * and give wrong results; serialize them. */
+lik_status lik_decode_attention_f16_noalloc(
+    const void* q, const void* k, const void* v, void* out,
+    int64_t batch, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim,
+    int64_t seqlen, int64_t kv_buf_len, float softmax_scale, void* stream);
+
 /* INT8 per-token KV: K = k_q * k_scale[token], V = v_q * v_scale[token].
  * Replaces launch_decode_attention_int8
  * (kernels/attention/fused_attention_int8.cu:109-122, declared

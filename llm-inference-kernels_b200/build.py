@@ -34,6 +34,7 @@ CU_SOURCES = {
     "decode.cu": [],
     "quantize.cu": ["-fmad=false"],   # bit-exact quantization: no contraction
     "cabi.cu": [],
+    "noalloc.cu": [],
 }
 HEADERS = ["lik_device.cuh", "lik_internal.h"]
 

@@ -26,6 +26,8 @@ cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 
 }  // namespace
 
+void set_last_error(const std::string& msg) { g_last_error = msg; }
+
 bool device_info(DeviceInfo& info, std::string& err) {
     static std::mutex mu;
     static DeviceInfo cache[64];

@@ -39,6 +39,9 @@ struct DeviceInfo {
 };
 bool device_info(DeviceInfo& info, std::string& err);
 
+// Record the calling thread's lik_last_error() text.
+void set_last_error(const std::string& msg);
+
 // Heads handled together by one work unit (a divisor of the GQA group size).
 int heads_per_unit(int64_t group, int fmt);
 

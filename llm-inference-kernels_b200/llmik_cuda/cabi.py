@@ -29,6 +29,7 @@ SIGNATURES = {
     "lik_workspace_init": (_int, [_p, _sz, _p]),
     "lik_workspace_check": (_int, [_p, _sz, _p, C.POINTER(_int)]),
     "lik_decode_attention_f16": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _f, _p, _sz, _p]),
+    "lik_decode_attention_f16_noalloc": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _f, _p]),
     "lik_decode_attention_int8": (_int, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _f,
                                          _p, _sz, _p]),
     "lik_decode_attention_int4": (_int, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
