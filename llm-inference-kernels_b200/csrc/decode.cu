@@ -93,8 +93,8 @@ struct DecodeParams {
     int n_heads, n_kv_heads, nhb;
     int group_size, tok_bulk, kg_smem, ngt;
     int n_ctas, nst, stage_bytes;
-    int off_v, off_ks, off_vs, off_vz, off_kgs, off_kgz;
-    int off_work, off_ml, off_misc, off_bar;
+    int off_v, off_ks, off_vs, off_vz, off_kgs, off_kgz, off_q;
+    int off_work, off_abuf, off_ml, off_misc, off_bar;
     float qscale;
     float* part;
     unsigned* counters;
@@ -199,6 +199,29 @@ __device__ __forceinline__ float h2_sum(half2 a) {
     return f.x + f.y;
 }
 
+// ---- optional timeline probes (diagnostic builds only: -DLIK_TIMELINE) ------
+#ifdef LIK_TIMELINE
+__device__ unsigned long long g_lik_timeline[4096 * 12];
+__device__ __forceinline__ void lik_tl(int slot) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    g_lik_timeline[blockIdx.x * 12 + slot] = t;
+    if (slot == 0) {
+        unsigned sm;
+        asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));
+        g_lik_timeline[blockIdx.x * 12 + 8] = sm;
+    }
+}
+#define LIK_TL(cond, slot) \
+    do {                   \
+        if (cond) lik_tl(slot); \
+    } while (0)
+#else
+#define LIK_TL(cond, slot) \
+    do {                   \
+    } while (0)
+#endif
+
 // ---- the kernel -----------------------------------------------------------
 
 template <int FMT, int HB>
@@ -233,6 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
         fence_barrier_init();
     }
     __syncthreads();
+    LIK_TL(tid == 0, 0);
 
     // ======================= producer warp ================================
     if (warp == kNCW) {
@@ -275,8 +299,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                     if (F::ZV) reinterpret_cast<__half*>(sb + p.off_vz)[t] = p.vz[rowbase + t];
                 }
             }
+            const bool new_unit = (j == 0 || ti == 0);
             if (lane == 0) {
-                uint32_t bytes = 2u * ntok * ROWB;
+                uint32_t bytes = 2u * ntok * ROWB + (new_unit ? HB * kHeadDim * 2 : 0);
                 int g0 = 0, ngrp = 0;
                 if ((F::TOKK || F::TOKV) && p.tok_bulk) {
                     bytes += (F::TOKK + F::TOKV + F::ZV) * n8 * 2;
@@ -288,6 +313,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                     bytes += (F::ZK ? 2 : 1) * ngrp * kHeadDim * 2;
                 }
                 mbar_arrive_expect_tx(&full[st], bytes);
+                if (new_unit) {
+                    const int hb = static_cast<int>(unit - bk * p.nhb);
+                    const long long b = bk / p.n_kv_heads;
+                    const long long kvh = bk - b * p.n_kv_heads;
+                    const long long qo = (b * p.n_heads + kvh * p.nhb * HB + hb * HB) * kHeadDim;
+                    bulk_g2s(sb + p.off_q, p.q + qo, HB * kHeadDim * 2, &full[st], pol);
+                }
                 bulk_g2s(sb, p.k + rowbase * ROWB, ntok * ROWB, &full[st], pol);
                 bulk_g2s(sb + p.off_v, p.v + rowbase * ROWB, ntok * ROWB, &full[st], pol);
                 if ((F::TOKK || F::TOKV) && p.tok_bulk) {
@@ -333,7 +365,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
     const int nct = kNCW * 32;
 
     uint16_t* pbuf = reinterpret_cast<uint16_t*>(smem + p.off_work) + w * TW * HB;  // p as f16
-    float* abuf = reinterpret_cast<float*>(smem + p.off_work);
+    float* abuf = reinterpret_cast<float*>(smem + p.off_abuf);
+    const long long first_unit_of_cta = tb / p.tpu;
     float* mlb = reinterpret_cast<float*>(smem + p.off_ml);
 
     float m_run = -INFINITY, l_run = 0.f;
@@ -353,8 +386,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
     long long unit = tb / p.tpu;
     long long ti = tb - unit * p.tpu;
     for (long long i = tb; i < te; ++i) {
-        if (unit != cur_unit) {
-            // ---- start of a unit segment: load q for the HB heads ----
+        const bool new_unit = (unit != cur_unit);
+        if (new_unit) {
+            // ---- start of a unit segment ----
             cur_unit = unit;
             seg_t0 = ti;
             cur_g = -1;
@@ -366,10 +400,26 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
             m_run = -INFINITY;
             l_run = 0.f;
 #pragma unroll
-            for (int h = 0; h < HB; ++h) {
+            for (int h = 0; h < HB; ++h)
 #pragma unroll
                 for (int c = 0; c < PVC; ++c) acc[h][c] = 0.f;
-                const __half* qp = p.q + qoff + h * kHeadDim;
+        }
+
+        if (!aborted) {
+            if (misc[0] || !mbar_wait_bounded(&full[st], ph)) {
+                aborted = true;
+                misc[0] = 1;
+                if (lane == 0) atomicExch(p.err, kDevWaitTimeout);
+            }
+        }
+        LIK_TL(tid == 0 && new_unit && i != tb, 11);
+        if (new_unit) {
+            // q for the HB heads arrived with this stage (the producer copies it
+            // into the first stage of every unit segment)
+            const __half* sq = reinterpret_cast<const __half*>(smem + static_cast<size_t>(st) * p.stage_bytes + p.off_q);
+#pragma unroll
+            for (int h = 0; h < HB; ++h) {
+                const __half* qp = sq + h * kHeadDim;
                 // the lane's 16 QK channels, as 16 halves in channel order
                 uint4 ua, ub;
                 if (FMT == kF16) {
@@ -400,14 +450,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                 }
             }
         }
-
-        if (!aborted) {
-            if (misc[0] || !mbar_wait_bounded(&full[st], ph)) {
-                aborted = true;
-                misc[0] = 1;
-                if (lane == 0) atomicExch(p.err, kDevWaitTimeout);
-            }
-        }
+        LIK_TL(tid == 0 && i == tb, 1);
 
         const long long t0 = ti * T;
         const int ntok = static_cast<int>(min(static_cast<long long>(T), p.seqlen - t0));
@@ -611,97 +654,152 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
         if (lane == 0) mbar_arrive(&empty[st]);
 
         // ---------------- end of a unit segment: merge and emit ----------------
+        // Every warp publishes its raw state; warp 0 alone combines the
+        // warps, writes the output (or a partial + ticket, and the cross-CTA
+        // merge when it completes the unit) while warps 1..7 go on streaming.
         if (ti == p.tpu - 1 || i == te - 1) {
+            LIK_TL(tid == 0 && i == te - 1, 4);
             if (PVC == 8) {
 #pragma unroll
                 for (int h = 0; h < HB; ++h)
 #pragma unroll
                     for (int c = 0; c < 8; ++c) acc[h][c] += __shfl_xor_sync(kFull, acc[h][c], 16);
             }
-            if (grp == 0 && prim) {
-                float* e = mlb + (w * HB + hh) * 3;
-                e[0] = m_run;
-                e[1] = l_run;
-            }
+            LIK_TL(tid == 0 && i != te - 1 && seg_t0 != 0 && false == (i == te - 1), 9);
+            // A: warp 0 has finished the previous segment's combine (it reads
+            // abuf / mlb) before anyone overwrites them.
             named_bar_sync(1, nct);
+            if (grp == 0 && prim) {
+                mlb[(w * HB + hh) * 3] = m_run;
+                mlb[(w * HB + hh) * 3 + 1] = l_run;
+            }
 #pragma unroll
             for (int h = 0; h < HB; ++h) {
-                float M = -INFINITY;
-                for (int ww = 0; ww < kNCW; ++ww) M = fmaxf(M, mlb[(ww * HB + h) * 3]);
-                const float f = fast_exp2(mlb[(w * HB + h) * 3] - M);
                 float* dst = abuf + (w * HB + h) * kHeadDim;
                 if (PVC == 4) {
                     *reinterpret_cast<float4*>(dst + lane * 4) =
-                        make_float4(acc[h][0] * f, acc[h][1] * f, acc[h][2] * f, acc[h][3] * f);
+                        make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
                 } else if (lane < 16) {
+                    *reinterpret_cast<float4*>(dst + lane * 8) =
+                        make_float4(acc[h][0], acc[h][2], acc[h][4], acc[h][6]);
+                    *reinterpret_cast<float4*>(dst + lane * 8 + 4) =
+                        make_float4(acc[h][1], acc[h][3], acc[h][5], acc[h][7]);
+                }
+            }
+            named_bar_sync(1, nct);  // B
+            LIK_TL(tid == 0 && i == te - 1, 5);
+            // All consumer warps combine the eight warp states and write the
+            // output (whole unit) or this CTA's partial. Only the completion
+            // ticket -- and, if this CTA completes the unit, the merge -- waits
+            // on global memory: done by warp 0 mid-stream (the other warps go
+            // on streaming) and by every warp on the CTA's last segment.
+            const bool final_seg = (i == te - 1);
+            {
+                float M[HB], L[HB];
 #pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        dst[lane * 8 + k] = acc[h][2 * k] * f;
-                        dst[lane * 8 + k + 4] = acc[h][2 * k + 1] * f;
-                    }
+                for (int h = 0; h < HB; ++h) {
+                    M[h] = -INFINITY;
+#pragma unroll
+                    for (int ww = 0; ww < kNCW; ++ww) M[h] = fmaxf(M[h], mlb[(ww * HB + h) * 3]);
+                    L[h] = 0.f;
+#pragma unroll
+                    for (int ww = 0; ww < kNCW; ++ww)
+                        L[h] = fmaf(mlb[(ww * HB + h) * 3 + 1], fast_exp2(mlb[(ww * HB + h) * 3] - M[h]), L[h]);
                 }
-            }
-            named_bar_sync(1, nct);
-            const bool whole = (seg_t0 == 0 && ti == p.tpu - 1);
-            const long long first_unit_of_cta = tb / p.tpu;
-            const long long slot = 2 * cta + (unit == first_unit_of_cta ? 0 : 1);
-            for (int o = tid; o < HB * kHeadDim; o += nct) {
-                const int h = o >> 7;
-                float M = -INFINITY;
-                for (int ww = 0; ww < kNCW; ++ww) M = fmaxf(M, mlb[(ww * HB + h) * 3]);
-                float L = 0.f, A = 0.f;
-                for (int ww = 0; ww < kNCW; ++ww) {
-                    const float* e = mlb + (ww * HB + h) * 3;
-                    L = fmaf(e[1], fast_exp2(e[0] - M), L);
-                    A += abuf[(ww * HB + h) * kHeadDim + (o & 127)];
-                }
+                auto pick = [&](const float (&x)[HB], int h) {
+                    float r = x[0];
+#pragma unroll
+                    for (int hx = 1; hx < HB; ++hx)
+                        if (h == hx) r = x[hx];
+                    return r;
+                };
+                auto combined = [&](int o) {
+                    const int h = o >> 7;
+                    const float mh = pick(M, h);
+                    float a = 0.f;
+#pragma unroll
+                    for (int ww = 0; ww < kNCW; ++ww)
+                        a = fmaf(fast_exp2(mlb[(ww * HB + h) * 3] - mh), abuf[(ww * HB + h) * kHeadDim + (o & 127)], a);
+                    return a;
+                };
+                const bool whole = (seg_t0 == 0 && ti == p.tpu - 1);
                 if (whole) {
-                    p.out[qoff + o] = __float2half_rn(A / L);
+                    for (int o = tid; o < HB * kHeadDim; o += nct)
+                        p.out[qoff + o] = __float2half_rn(combined(o) / pick(L, o >> 7));
                 } else {
+                    const long long slot = 2 * cta + (unit == first_unit_of_cta ? 0 : 1);
                     float* sp = p.part + slot * SL;
-                    sp[o] = A;
-                    if ((o & 127) == 0) {
-                        sp[HB * kHeadDim + h] = M;
-                        sp[HB * kHeadDim + HB + h] = L;
+                    for (int o = tid; o < HB * kHeadDim; o += nct) sp[o] = combined(o);
+                    if (tid < HB) {
+                        sp[HB * kHeadDim + tid] = pick(M, tid);
+                        sp[HB * kHeadDim + HB + tid] = pick(L, tid);
                     }
+                    named_bar_sync(1, nct);  // C: the whole partial is written
                 }
             }
-            if (!whole) {
-                __threadfence();
-                named_bar_sync(1, nct);
-                const long long c_lo = owner_cta(unit * p.tpu, p.total_tiles, p.n_ctas);
-                const long long c_hi = owner_cta((unit + 1) * p.tpu - 1, p.total_tiles, p.n_ctas);
-                if (tid == 0) {
-                    const unsigned nseg = static_cast<unsigned>(c_hi - c_lo + 1);
-                    const unsigned old = atomicAdd(&p.counters[unit], 1u);
-                    const int last = (old == nseg - 1);
-                    if (last) p.counters[unit] = 0u;
-                    misc[1] = last;
-                }
-                named_bar_sync(1, nct);
-                if (misc[1]) {
-                    __threadfence();
-                    for (int o = tid; o < HB * kHeadDim; o += nct) {
-                        const int h = o >> 7;
-                        float M = -INFINITY;
-                        for (long long c2 = c_lo; c2 <= c_hi; ++c2) {
-                            const long long fu = cta_first_tile(c2, p.total_tiles, p.n_ctas) / p.tpu;
-                            const float* sp = p.part + (2 * c2 + (fu == unit ? 0 : 1)) * SL;
-                            M = fmaxf(M, __ldcg(sp + HB * kHeadDim + h));
+            LIK_TL(tid == 0 && i != te - 1 && seg_t0 != 0, 10);
+            const bool whole = (seg_t0 == 0 && ti == p.tpu - 1);
+            if (!whole && (final_seg || w == 0)) {
+                const int wl = final_seg ? tid : lane;
+                const int nw = final_seg ? nct : 32;
+                {
+                    const long long c_lo = owner_cta(unit * p.tpu, p.total_tiles, p.n_ctas);
+                    const long long c_hi = owner_cta((unit + 1) * p.tpu - 1, p.total_tiles, p.n_ctas);
+                    int last = 0;
+                    if (wl == 0) {
+                        // release this CTA's partial / acquire the others' (cumulative
+                        // over barrier C)
+                        const unsigned old = atomic_add_acq_rel_gpu(&p.counters[unit], 1u);
+                        last = (old == static_cast<unsigned>(c_hi - c_lo));
+                        if (last) p.counters[unit] = 0u;
+                    }
+                    if (final_seg) {
+                        if (wl == 0) misc[1] = last;
+                        named_bar_sync(1, nct);
+                        last = misc[1];
+                    } else {
+                        last = __shfl_sync(kFull, last, 0);
+                        __syncwarp();
+                    }
+                    LIK_TL(tid == 0 && i == te - 1, 6);
+                    if (last) {
+                        // CTA c_lo's segment sits in its second slot unless its
+                        // range starts exactly at this unit's first tile; every
+                        // later CTA's segment is its first unit (slot 0).
+                        const bool lo_first = cta_first_tile(c_lo, p.total_tiles, p.n_ctas) == unit * p.tpu;
+                        const int nseg = static_cast<int>(c_hi - c_lo + 1);
+                        for (int o = wl; o < HB * kHeadDim; o += nw) {
+                            const int h = o >> 7;
+                            float mg = -INFINITY, lg = 0.f, ag = 0.f;
+                            constexpr int SB = 4;  // segments whose loads are issued together
+                            for (int s0 = 0; s0 < nseg; s0 += SB) {
+                                float ms[SB], ls[SB], as[SB];
+#pragma unroll
+                                for (int k = 0; k < SB; ++k) {
+                                    const long long c2 = c_lo + s0 + k;
+                                    const bool ok = s0 + k < nseg;
+                                    const float* q2 =
+                                        p.part + (2 * (ok ? c2 : c_lo) + ((ok && c2 == c_lo && !lo_first) ? 1 : 0)) * SL;
+                                    ms[k] = ok ? __ldcg(q2 + HB * kHeadDim + h) : -INFINITY;
+                                    ls[k] = ok ? __ldcg(q2 + HB * kHeadDim + HB + h) : 0.f;
+                                    as[k] = ok ? __ldcg(q2 + o) : 0.f;
+                                }
+#pragma unroll
+                                for (int k = 0; k < SB; ++k) {
+                                    const float mn = fmaxf(mg, ms[k]);
+                                    const float fa = fast_exp2(mg - mn);
+                                    const float fb = fast_exp2(ms[k] - mn);
+                                    lg = lg * fa + ls[k] * fb;
+                                    ag = ag * fa + as[k] * fb;
+                                    mg = mn;
+                                }
+                            }
+                            p.out[qoff + o] = __float2half_rn(ag / lg);
                         }
-                        float L = 0.f, A = 0.f;
-                        for (long long c2 = c_lo; c2 <= c_hi; ++c2) {
-                            const long long fu = cta_first_tile(c2, p.total_tiles, p.n_ctas) / p.tpu;
-                            const float* sp = p.part + (2 * c2 + (fu == unit ? 0 : 1)) * SL;
-                            const float f = fast_exp2(__ldcg(sp + HB * kHeadDim + h) - M);
-                            L = fmaf(__ldcg(sp + HB * kHeadDim + HB + h), f, L);
-                            A = fmaf(__ldcg(sp + o), f, A);
-                        }
-                        p.out[qoff + o] = __float2half_rn(A / L);
                     }
                 }
+                LIK_TL(tid == 0 && i == te - 1, 7);
             }
-            named_bar_sync(1, nct);
         }
         if (++st == p.nst) {
             st = 0;
@@ -711,7 +809,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
             ti = 0;
             ++unit;
         }
+        LIK_TL(tid == 0 && i == te - 2, 2);
     }
+    LIK_TL(tid == 0, 3);
 }
 
 // ---- host side ------------------------------------------------------------
@@ -795,10 +895,15 @@ lik_status launch_t(const DecodeArgs& a, const DeviceInfo& di, cudaStream_t stre
     off += p.ngt * kHeadDim * 2;
     p.off_kgz = off;
     if (F::ZK) off += p.ngt * kHeadDim * 2;
+    off = static_cast<int>(align_up(off, 16));
+    p.off_q = off;
+    off += HB * kHeadDim * 2;
     p.stage_bytes = static_cast<int>(align_up(off, 128));
 
-    const int work = static_cast<int>(std::max<size_t>(static_cast<size_t>(kNCW) * (T / kNCW) * HB * 4,
-                                                       static_cast<size_t>(kNCW) * HB * kHeadDim * 4));
+    // per-warp fp16 softmax weights, then the per-warp raw accumulators
+    const int pbuf_bytes = static_cast<int>(align_up(static_cast<size_t>(kNCW) * (T / kNCW) * HB * 2, 16));
+    const int abuf_bytes = kNCW * HB * kHeadDim * 4;
+    const int work = pbuf_bytes + abuf_bytes;
     const int fixed = work + kNCW * HB * 3 * 4 + 64 + 2 * 8 * 8;
     int nst = (di.max_smem_optin - fixed - 256) / p.stage_bytes;
     nst = std::min(nst, 8);
@@ -810,6 +915,7 @@ lik_status launch_t(const DecodeArgs& a, const DeviceInfo& di, cudaStream_t stre
     p.nst = nst;
     size_t o2 = static_cast<size_t>(nst) * p.stage_bytes;
     p.off_work = static_cast<int>(o2);
+    p.off_abuf = static_cast<int>(o2 + pbuf_bytes);
     o2 += work;
     p.off_ml = static_cast<int>(o2);
     o2 += kNCW * HB * 3 * 4;

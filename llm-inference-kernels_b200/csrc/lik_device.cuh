@@ -82,6 +82,17 @@ __device__ __forceinline__ uint64_t l2_policy_evict_first() {
     return pol;
 }
 
+// GPU-scope acquire-release fence (cumulative: covers the warp's writes
+// ordered before it by __syncwarp).
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
+// atom.add with acquire-release semantics at GPU scope; returns the old value.
+__device__ __forceinline__ unsigned atomic_add_acq_rel_gpu(unsigned* p, unsigned v) {
+    unsigned old;
+    asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
