@@ -119,13 +119,6 @@ __device__ __forceinline__ int lane_of_head(int h) {
     return lane;
 }
 
-// True for the one lane per (8-lane group, head) whose non-split lane bits are 0.
-template <int HB>
-__device__ __forceinline__ bool head_primary(int lane) {
-    constexpr int used = HB >= 8 ? 3 : HB >= 4 ? 2 : HB >= 2 ? 1 : 0;
-    return ((lane & 7) >> used) == 0;
-}
-
 // Sum v[0..HB) over the 8 lanes of a group (lane bits 0..2), scattering heads:
 // afterwards the lane holds the full sum of head head_of_lane<HB>(lane).
 template <int HB>
@@ -360,8 +353,18 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
     const int w = warp;
     const int grp = lane >> 3;
     const int jl = lane & 7;
-    const int hh = head_of_lane<HB>(lane);
-    const bool prim = head_primary<HB>(lane);
+    // QK reduce-scatter layout: QG passes of HB heads reduced together; lane
+    // bits [0, log2 QG) select the pass, the next bits the head, the rest of
+    // the 8-lane group holds duplicates (only when QG * HB < 8).
+    constexpr int QG = (8 / HB) < NP ? (8 / HB) : NP;
+    constexpr int QV = QG * HB;
+    constexpr int NGRP = NP / QG;
+    static_assert(NP % QG == 0, "passes must group evenly");
+    constexpr int LQG = QG >= 8 ? 3 : QG >= 4 ? 2 : QG >= 2 ? 1 : 0;
+    constexpr int LQV = QV >= 8 ? 3 : QV >= 4 ? 2 : QV >= 2 ? 1 : 0;
+    const int qpl = head_of_lane<QG>(lane & 7);            // pass within the group
+    const int hh = head_of_lane<HB>((lane & 7) >> LQG);     // head
+    const bool prim = ((lane & 7) >> LQV) == 0;            // not a duplicate
     const int nct = kNCW * 32;
 
     uint16_t* pbuf = reinterpret_cast<uint16_t*>(smem + p.off_work) + w * TW * HB;  // p as f16
@@ -468,124 +471,135 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
             // ---------------- QK ----------------
             // K is dequantized to fp16 with the oracle's rounding (fp16(code *
             // scale [+ zero])); products f16 x f16 are exact, sums in fp32.
-            float sc[NP];
+            // Passes (4 positions each) are processed QG at a time so that,
+            // after the 8-lane reduce-scatter of QG*HB partial sums, every lane
+            // holds exactly one distinct (position, head) score.
+            float sc[NGRP];
 #pragma unroll
-            for (int pp = 0; pp < NP; ++pp) {
-                const int tt = wt0 + pp * 4 + grp;
-                float part[HB];
+            for (int gq = 0; gq < NGRP; ++gq) {
+                float vals[QV];
 #pragma unroll
-                for (int h = 0; h < HB; ++h) part[h] = 0.f;
-                if (tt < ntok) {
-                    const uint8_t* row = sK + tt * ROWB;
-                    uint32_t kk[8];
-                    if (FMT == kF16) {
-                        const uint4 ka = *reinterpret_cast<const uint4*>(row + jl * 16);
-                        const uint4 kb = *reinterpret_cast<const uint4*>(row + 128 + jl * 16);
-                        kk[0] = ka.x; kk[1] = ka.y; kk[2] = ka.z; kk[3] = ka.w;
-                        kk[4] = kb.x; kk[5] = kb.y; kk[6] = kb.z; kk[7] = kb.w;
-                    } else if (FMT == kI8) {
-                        // raw codes; the token scale multiplies the reduced score
-                        const uint4 ka = *reinterpret_cast<const uint4*>(row + jl * 16);
-                        half2 a0, a1;
-                        i8x4_to_h2(ka.x, a0, a1); kk[0] = as_u32(a0); kk[1] = as_u32(a1);
-                        i8x4_to_h2(ka.y, a0, a1); kk[2] = as_u32(a0); kk[3] = as_u32(a1);
-                        i8x4_to_h2(ka.z, a0, a1); kk[4] = as_u32(a0); kk[5] = as_u32(a1);
-                        i8x4_to_h2(ka.w, a0, a1); kk[6] = as_u32(a0); kk[7] = as_u32(a1);
-                    } else {
-                        const int tabs = static_cast<int>(t0) + tt;
-                        if (cur_g < 0 || tabs >= gnext) {
-                            const int g = tabs / p.group_size;
-                            cur_g = g;
-                            gnext = (g + 1) * p.group_size;
-                            const __half* gsp;
-                            const __half* gzp = nullptr;
-                            if (p.kg_smem) {
-                                const int g0 = static_cast<int>(t0) / p.group_size;
-                                gsp = reinterpret_cast<const __half*>(sb + p.off_kgs) + (g - g0) * kHeadDim;
-                                if (F::ZK) gzp = reinterpret_cast<const __half*>(sb + p.off_kgz) + (g - g0) * kHeadDim;
-                            } else {
-                                const long long gb = (bk * p.ng_buf + g) * kHeadDim;
-                                gsp = p.ks + gb;
-                                if (F::ZK) gzp = p.kz + gb;
-                            }
-                            const uint4 s0 = *reinterpret_cast<const uint4*>(gsp + 16 * jl);
-                            const uint4 s1 = *reinterpret_cast<const uint4*>(gsp + 16 * jl + 8);
-                            const __half* sh0 = reinterpret_cast<const __half*>(&s0);
-                            const __half* sh1 = reinterpret_cast<const __half*>(&s1);
+                for (int pl2 = 0; pl2 < QG; ++pl2) {
+                    const int tt = wt0 + (gq * QG + pl2) * 4 + grp;
+                    float part[HB], part2[HB];
 #pragma unroll
-                            for (int k = 0; k < 4; ++k) {
-                                kg[k] = as_u32(__halves2half2(sh0[k], sh0[k + 4]));
-                                kg[4 + k] = as_u32(__halves2half2(sh1[k], sh1[k + 4]));
-                            }
-                            if (F::ZK) {
-                                const uint4 z0 = *reinterpret_cast<const uint4*>(gzp + 16 * jl);
-                                const uint4 z1 = *reinterpret_cast<const uint4*>(gzp + 16 * jl + 8);
-                                const __half* zh0 = reinterpret_cast<const __half*>(&z0);
-                                const __half* zh1 = reinterpret_cast<const __half*>(&z1);
-#pragma unroll
+                    for (int h = 0; h < HB; ++h) part[h] = part2[h] = 0.f;
+                    if (tt < ntok) {
+                        const uint8_t* row = sK + tt * ROWB;
+                        uint32_t kk[8];
+                        if (FMT == kF16) {
+                            const uint4 ka = *reinterpret_cast<const uint4*>(row + jl * 16);
+                            const uint4 kb = *reinterpret_cast<const uint4*>(row + 128 + jl * 16);
+                            kk[0] = ka.x; kk[1] = ka.y; kk[2] = ka.z; kk[3] = ka.w;
+                            kk[4] = kb.x; kk[5] = kb.y; kk[6] = kb.z; kk[7] = kb.w;
+                        } else if (FMT == kI8) {
+                            // raw codes; the token scale multiplies the reduced score
+                            const uint4 ka = *reinterpret_cast<const uint4*>(row + jl * 16);
+                            half2 a0, a1;
+                            i8x4_to_h2(ka.x, a0, a1); kk[0] = as_u32(a0); kk[1] = as_u32(a1);
+                            i8x4_to_h2(ka.y, a0, a1); kk[2] = as_u32(a0); kk[3] = as_u32(a1);
+                            i8x4_to_h2(ka.z, a0, a1); kk[4] = as_u32(a0); kk[5] = as_u32(a1);
+                            i8x4_to_h2(ka.w, a0, a1); kk[6] = as_u32(a0); kk[7] = as_u32(a1);
+                        } else {
+                            const int tabs = static_cast<int>(t0) + tt;
+                            if (cur_g < 0 || tabs >= gnext) {
+                                const int g = tabs / p.group_size;
+                                cur_g = g;
+                                gnext = (g + 1) * p.group_size;
+                                const __half* gsp;
+                                const __half* gzp = nullptr;
+                                if (p.kg_smem) {
+                                    const int g0 = static_cast<int>(t0) / p.group_size;
+                                    gsp = reinterpret_cast<const __half*>(sb + p.off_kgs) + (g - g0) * kHeadDim;
+                                    if (F::ZK) gzp = reinterpret_cast<const __half*>(sb + p.off_kgz) + (g - g0) * kHeadDim;
+                                } else {
+                                    const long long gb = (bk * p.ng_buf + g) * kHeadDim;
+                                    gsp = p.ks + gb;
+                                    if (F::ZK) gzp = p.kz + gb;
+                                }
+                                const uint4 s0 = *reinterpret_cast<const uint4*>(gsp + 16 * jl);
+                                const uint4 s1 = *reinterpret_cast<const uint4*>(gsp + 16 * jl + 8);
+                                const __half* sh0 = reinterpret_cast<const __half*>(&s0);
+                                const __half* sh1 = reinterpret_cast<const __half*>(&s1);
+    #pragma unroll
                                 for (int k = 0; k < 4; ++k) {
-                                    kgz[k] = as_u32(__halves2half2(zh0[k], zh0[k + 4]));
-                                    kgz[4 + k] = as_u32(__halves2half2(zh1[k], zh1[k + 4]));
+                                    kg[k] = as_u32(__halves2half2(sh0[k], sh0[k + 4]));
+                                    kg[4 + k] = as_u32(__halves2half2(sh1[k], sh1[k + 4]));
+                                }
+                                if (F::ZK) {
+                                    const uint4 z0 = *reinterpret_cast<const uint4*>(gzp + 16 * jl);
+                                    const uint4 z1 = *reinterpret_cast<const uint4*>(gzp + 16 * jl + 8);
+                                    const __half* zh0 = reinterpret_cast<const __half*>(&z0);
+                                    const __half* zh1 = reinterpret_cast<const __half*>(&z1);
+    #pragma unroll
+                                    for (int k = 0; k < 4; ++k) {
+                                        kgz[k] = as_u32(__halves2half2(zh0[k], zh0[k + 4]));
+                                        kgz[4 + k] = as_u32(__halves2half2(zh1[k], zh1[k + 4]));
+                                    }
+                                }
+                            }
+                            const uint2 kw = *reinterpret_cast<const uint2*>(row + jl * 8);
+                            half2 c0[4], c1[4];
+                            i4x8_to_h2<F::SIGNED>(kw.x, c0);
+                            i4x8_to_h2<F::SIGNED>(kw.y, c1);
+    #pragma unroll
+                            for (int k = 0; k < 4; ++k) {
+                                if (F::ZK) {
+                                    kk[k] = as_u32(__hfma2(c0[k], as_h2(kg[k]), as_h2(kgz[k])));
+                                    kk[4 + k] = as_u32(__hfma2(c1[k], as_h2(kg[4 + k]), as_h2(kgz[4 + k])));
+                                } else {
+                                    kk[k] = as_u32(__hmul2(c0[k], as_h2(kg[k])));
+                                    kk[4 + k] = as_u32(__hmul2(c1[k], as_h2(kg[4 + k])));
                                 }
                             }
                         }
-                        const uint2 kw = *reinterpret_cast<const uint2*>(row + jl * 8);
-                        half2 c0[4], c1[4];
-                        i4x8_to_h2<F::SIGNED>(kw.x, c0);
-                        i4x8_to_h2<F::SIGNED>(kw.y, c1);
 #pragma unroll
-                        for (int k = 0; k < 4; ++k) {
-                            if (F::ZK) {
-                                kk[k] = as_u32(__hfma2(c0[k], as_h2(kg[k]), as_h2(kgz[k])));
-                                kk[4 + k] = as_u32(__hfma2(c1[k], as_h2(kg[4 + k]), as_h2(kgz[4 + k])));
-                            } else {
-                                kk[k] = as_u32(__hmul2(c0[k], as_h2(kg[k])));
-                                kk[4 + k] = as_u32(__hmul2(c1[k], as_h2(kg[4 + k])));
-                            }
-                        }
+                        for (int c = 0; c < 8; ++c)
+#pragma unroll
+                            for (int h = 0; h < HB; ++h) fma_h2_2acc(qh[h][c], kk[c], part[h], part2[h]);
                     }
-                    float part2[HB];
 #pragma unroll
-                    for (int h = 0; h < HB; ++h) part2[h] = 0.f;
-#pragma unroll
-                    for (int c = 0; c < 8; ++c)
-#pragma unroll
-                        for (int h = 0; h < HB; ++h) fma_h2_2acc(qh[h][c], kk[c], part[h], part2[h]);
-#pragma unroll
-                    for (int h = 0; h < HB; ++h) part[h] += part2[h];
+                    for (int h = 0; h < HB; ++h) vals[pl2 * HB + h] = part[h] + part2[h];
                 }
-                float s = reduce_scatter8<HB>(part, lane);
+                float s = reduce_scatter8<QV>(vals, lane);
+                const int tt = wt0 + (gq * QG + qpl) * 4 + grp;
                 if (tt >= ntok) {
                     s = -INFINITY;
                 } else if (F::TOKK) {
                     s *= __half2float(sks[tt]);
                 }
-                sc[pp] = s;
+                sc[gq] = s;
             }
 
             // ---------------- online softmax (log2 domain) ----------------
+            // lanes sharing a head differ in the pass bits (xor 1 .. QG/2) and
+            // the position-group bits (xor 8, 16)
             float mloc = sc[0];
 #pragma unroll
-            for (int pp = 1; pp < NP; ++pp) mloc = fmaxf(mloc, sc[pp]);
+            for (int gq = 1; gq < NGRP; ++gq) mloc = fmaxf(mloc, sc[gq]);
+#pragma unroll
+            for (int m = 1; m < QG; m <<= 1) mloc = fmaxf(mloc, __shfl_xor_sync(kFull, mloc, m));
             mloc = fmaxf(mloc, __shfl_xor_sync(kFull, mloc, 8));
             mloc = fmaxf(mloc, __shfl_xor_sync(kFull, mloc, 16));
             const float mnew = fmaxf(m_run, mloc);
             const float alpha = fast_exp2(m_run - mnew);
             float ls = 0.f;
 #pragma unroll
-            for (int pp = 0; pp < NP; ++pp) {
-                const int tl = pp * 4 + grp;  // position within the warp's share
-                const float e = fast_exp2(sc[pp] - mnew);
+            for (int gq = 0; gq < NGRP; ++gq) {
+                const int tl = (gq * QG + qpl) * 4 + grp;  // position within the warp's share
+                const float e = fast_exp2(sc[gq] - mnew);
                 ls += e;
                 if (tl < nval && prim) pbuf[tl * HB + hh] = __half_as_ushort(__float2half_rn(e));
             }
+#pragma unroll
+            for (int m = 1; m < QG; m <<= 1) ls += __shfl_xor_sync(kFull, ls, m);
             ls += __shfl_xor_sync(kFull, ls, 8);
             ls += __shfl_xor_sync(kFull, ls, 16);
             l_run = fmaf(l_run, alpha, ls);
             m_run = mnew;
             float al[HB];
 #pragma unroll
-            for (int h = 0; h < HB; ++h) al[h] = __shfl_sync(kFull, alpha, lane_of_head<HB>(h));
+            for (int h = 0; h < HB; ++h) al[h] = __shfl_sync(kFull, alpha, lane_of_head<HB>(h) * QG);
             __syncwarp();
 #pragma unroll
             for (int h = 0; h < HB; ++h)
@@ -669,7 +683,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
             // A: warp 0 has finished the previous segment's combine (it reads
             // abuf / mlb) before anyone overwrites them.
             named_bar_sync(1, nct);
-            if (grp == 0 && prim) {
+            if (grp == 0 && prim && qpl == 0) {
                 mlb[(w * HB + hh) * 3] = m_run;
                 mlb[(w * HB + hh) * 3 + 1] = l_run;
             }
