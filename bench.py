@@ -75,6 +75,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-c4", action="store_true", help="skip the config-4 lines")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    ap.add_argument("--profile", action="store_true",
+                    help="profiler-friendly run: one warm replay, short e2e legs (timings not for reporting)")
     return ap.parse_args()
 
 
@@ -268,7 +270,7 @@ def copies_for(nbytes, l2):
     return max(1, math.ceil(3 * l2 / nbytes))
 
 
-def time_graph(torch, wl, steps, warmup, barrier, min_warm_s=1.0):
+def time_graph(torch, wl, steps, warmup, barrier, min_warm_s=1.0, max_warm=10000):
     """Capture `steps` steps in one CUDA graph; warm up; replay once timed.
     Returns device ms per step on this rank."""
     s = torch.cuda.Stream()
@@ -288,7 +290,7 @@ def time_graph(torch, wl, steps, warmup, barrier, min_warm_s=1.0):
         g.replay()
         torch.cuda.synchronize()
         n += 1
-        if n > 10000:
+        if n >= max_warm:
             break
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
@@ -332,13 +334,16 @@ def measured_hbm_peak():
 
 
 def ncu_traffic():
-    """Per-launch DRAM bytes of the fp16 config-1 kernel from the committed
-    ncu summary (profiles/decode_f16_config1.json), if present."""
+    """Per-launch DRAM bytes (read + write) of the fp16 config-1 kernel, from the
+    committed ncu summary profiles/decode_f16_config1.md, if present."""
     try:
-        with open(os.path.join(ROOT, "profiles", "decode_f16_config1.json")) as f:
-            return json.load(f).get("dram_bytes_per_launch")
+        with open(os.path.join(ROOT, "profiles", "decode_f16_config1.md")) as f:
+            for line in f:
+                if line.startswith("dram_bytes_per_launch:"):
+                    return int(line.split(":", 1)[1].strip())
     except (OSError, ValueError):
-        return None
+        pass
+    return None
 
 
 def check_against_oracle(out, q, k, v, units, what):
@@ -457,7 +462,9 @@ def run_ours(args):
         if fmt == "f16":
             q, k, v = wl.sets[0]
             check_against_oracle(wl.step(0), q, k, v, [0, b - 1], "config-1 fp16")
-        ms = max_over_ranks(torch, time_graph(torch, wl, steps, warmup, barrier), world)
+        ms = max_over_ranks(torch, time_graph(torch, wl, steps, warmup, barrier,
+                                              min_warm_s=0.0 if args.profile else 1.0,
+                                              max_warm=1 if args.profile else 10000), world)
         formats[name] = {"us_per_step": ms * 1e3, "TB_s": world * nb / (ms * 1e-3) / 1e12,
                          "bytes_per_step_per_gpu": nb, "copies_rotated": len(wl.sets)}
         if fmt == "f16":
@@ -500,10 +507,11 @@ def run_ours(args):
     clocks = sampler.stop()
 
     # ---- end to end through the public op (host buffers) ----
-    e2e_steps = max(3, min(steps, 20))
+    e2e_steps = 3 if args.profile else max(3, min(steps, 20))
     e2e_ms, h2d, d2h = e2e_host_buffers(torch, L, dev, e2e_steps)
     e2e_ms = max_over_ranks(torch, e2e_ms, world)
-    dec_ms = max_over_ranks(torch, e2e_decode_step(torch, L, dev, max(10, min(steps, 200))), world)
+    dec_ms = max_over_ranks(torch, e2e_decode_step(torch, L, dev, 3 if args.profile else max(10, min(steps, 200))),
+                            world)
 
     nb1 = algo_bytes("f16", b, s)
     value = world * nb1 / (head_ms * 1e-3) / 1e12
