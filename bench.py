@@ -307,12 +307,8 @@ def time_graph(torch, wl, steps, warmup, barrier, min_warm_s=1.0, max_warm=10000
 
 
 def max_over_ranks(torch, x, world):
-    if world == 1:
-        return x
-    import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    from llmik_cuda.shard import max_over_ranks as _max
+    return _max(x, device="cuda") if world > 1 else x
 
 
 def physical_index(local: int) -> int:
@@ -435,8 +431,9 @@ def run_ours(args):
     dist = None
     if world > 1:
         import torch.distributed as dist
+        os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep stdout to the one JSON line
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl")
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local if world > 1 else 0)
     torch.cuda.set_device(dev)
     import llmik_cuda as L
@@ -489,12 +486,8 @@ def run_ours(args):
             if fmt == "f16":
                 # assemble the output shards (NCCL all-gather, off the timed path)
                 # and check the last sequence against the oracle on rank 0
-                out = wl.step(0)
-                full = out
-                if dist is not None:
-                    parts = [torch.empty_like(out) for _ in range(world)]
-                    dist.all_gather(parts, out)
-                    full = torch.cat(parts)
+                from llmik_cuda.shard import gather_shards
+                full = gather_shards(wl.step(0))
                 if rank == 0:
                     bl_last = C4["batch"] - 1
                     kk, vv = make_slabs(torch, dev, 1, C4["seqlen"], bl_last * HKV, 2000, False)
