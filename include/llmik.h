@@ -202,6 +202,35 @@ lik_status lik_quantize_k_per_channel_groupwise_int4_asym(
     int64_t group_size, int64_t dst_pos, int64_t dst_buf_len, int64_t n_groups_buf,
     void* stream);
 
+/* ---- dequantize to fp16 (prefill / materialize) ---------------------- */
+/*
+ * Codes of the first `seqlen` positions of caches with allocated length
+ * kv_buf_len -> contiguous fp16 K and V [batch, n_kv_heads, seqlen, head_dim],
+ * each value fp16(code * scale [+ zero]) -- the rounding of the reference's
+ * dequantize helpers. Replaces the PyTorch materialize path
+ * Int4KIVICache._materialize_fp16 (integration/kv_int4_cache.py:226-245,
+ * helpers :41-67) and the test-side dequantization of INT8 caches
+ * (tests/test_kv_cache.py:282-283).
+ */
+lik_status lik_dequantize_int8(
+    const int8_t* k_q, const void* k_scale, const int8_t* v_q, const void* v_scale,
+    void* k_out, void* v_out, int64_t batch, int64_t n_kv_heads, int64_t seqlen,
+    int64_t kv_buf_len, int64_t head_dim, void* stream);
+
+lik_status lik_dequantize_int4(
+    const int8_t* k_q, const void* k_scale, const int8_t* v_q, const void* v_scale,
+    void* k_out, void* v_out, int64_t batch, int64_t n_kv_heads, int64_t seqlen,
+    int64_t kv_buf_len, int64_t head_dim, int64_t group_size, int64_t n_groups_buf,
+    void* stream);
+
+/* Asymmetric INT4 KIVI variant (no reference counterpart). */
+lik_status lik_dequantize_int4_asym(
+    const int8_t* k_q, const void* k_scale, const void* k_zero,
+    const int8_t* v_q, const void* v_scale, const void* v_zero,
+    void* k_out, void* v_out, int64_t batch, int64_t n_kv_heads, int64_t seqlen,
+    int64_t kv_buf_len, int64_t head_dim, int64_t group_size, int64_t n_groups_buf,
+    void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

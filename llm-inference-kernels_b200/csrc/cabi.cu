@@ -307,4 +307,50 @@ lik_status lik_quantize_k_per_channel_groupwise_int4_asym(const void* x, int8_t*
                         dst_buf_len, n_groups_buf, stream);
 }
 
+static lik_status dequant_common(int fmt, const void* kq, const void* ks, const void* kz, const void* vq,
+                                 const void* vs, const void* vz, void* ko, void* vo, int64_t batch, int64_t n_kv_heads,
+                                 int64_t seqlen, int64_t kv_buf_len, int64_t head_dim, int64_t group_size,
+                                 int64_t n_groups_buf, void* stream) {
+    if (batch < 0 || n_kv_heads <= 0 || seqlen < 0 || kv_buf_len < seqlen)
+        return fail(LIK_ERR_INVALID_ARGUMENT, "need batch >= 0, n_kv_heads > 0, 0 <= seqlen <= kv_buf_len");
+    if (head_dim != kHeadDim) return fail(LIK_ERR_UNSUPPORTED, "only head_dim=128 supported");
+    if (batch * seqlen == 0) return LIK_OK;
+    if (!kq || !ks || !vq || !vs || !ko || !vo || (fmt == 2 && (!kz || !vz)))
+        return fail(LIK_ERR_INVALID_ARGUMENT, "null tensor pointer");
+    if (!aligned16(kq) || !aligned16(vq) || !aligned16(ko) || !aligned16(vo))
+        return fail(LIK_ERR_MISALIGNED, "codes and outputs must be 16-byte aligned");
+    if (fmt != 0) {
+        if (group_size <= 0) return fail(LIK_ERR_INVALID_ARGUMENT, "group_size must be > 0");
+        if ((seqlen + group_size - 1) / group_size > n_groups_buf)
+            return fail(LIK_ERR_INVALID_ARGUMENT, "k_scale has fewer groups than ceil(seqlen / group_size)");
+    }
+    std::string err;
+    const lik_status s = launch_dequant(fmt, kq, ks, kz, vq, vs, vz, ko, vo, batch * n_kv_heads, seqlen, kv_buf_len,
+                                        group_size, n_groups_buf, as_stream(stream), err);
+    return s == LIK_OK ? s : fail(s, err);
+}
+
+lik_status lik_dequantize_int8(const int8_t* k_q, const void* k_scale, const int8_t* v_q, const void* v_scale,
+                               void* k_out, void* v_out, int64_t batch, int64_t n_kv_heads, int64_t seqlen,
+                               int64_t kv_buf_len, int64_t head_dim, void* stream) {
+    return dequant_common(0, k_q, k_scale, nullptr, v_q, v_scale, nullptr, k_out, v_out, batch, n_kv_heads, seqlen,
+                          kv_buf_len, head_dim, 0, 0, stream);
+}
+
+lik_status lik_dequantize_int4(const int8_t* k_q, const void* k_scale, const int8_t* v_q, const void* v_scale,
+                               void* k_out, void* v_out, int64_t batch, int64_t n_kv_heads, int64_t seqlen,
+                               int64_t kv_buf_len, int64_t head_dim, int64_t group_size, int64_t n_groups_buf,
+                               void* stream) {
+    return dequant_common(1, k_q, k_scale, nullptr, v_q, v_scale, nullptr, k_out, v_out, batch, n_kv_heads, seqlen,
+                          kv_buf_len, head_dim, group_size, n_groups_buf, stream);
+}
+
+lik_status lik_dequantize_int4_asym(const int8_t* k_q, const void* k_scale, const void* k_zero, const int8_t* v_q,
+                                    const void* v_scale, const void* v_zero, void* k_out, void* v_out, int64_t batch,
+                                    int64_t n_kv_heads, int64_t seqlen, int64_t kv_buf_len, int64_t head_dim,
+                                    int64_t group_size, int64_t n_groups_buf, void* stream) {
+    return dequant_common(2, k_q, k_scale, k_zero, v_q, v_scale, v_zero, k_out, v_out, batch, n_kv_heads, seqlen,
+                          kv_buf_len, head_dim, group_size, n_groups_buf, stream);
+}
+
 }  // extern "C"

@@ -60,6 +60,11 @@ lik_status launch_quant_kgroup(bool asym, const void* x, void* codes, void* scal
                                int64_t dst_pos, int64_t dst_buf_len, int64_t n_groups_buf,
                                cudaStream_t stream, std::string& err);
 
+lik_status launch_dequant(int fmt, const void* kq, const void* ks, const void* kz, const void* vq, const void* vs,
+                          const void* vz, void* kout, void* vout, int64_t n_slabs, int64_t seqlen,
+                          int64_t kv_buf_len, int64_t group_size, int64_t n_groups_buf, cudaStream_t stream,
+                          std::string& err);
+
 constexpr int kHeadDim = 128;
 
 // Workspace layout shared by host and device code.

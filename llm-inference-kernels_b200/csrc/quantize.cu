@@ -287,3 +287,112 @@ lik_status launch_quant_kgroup(bool asym, const void* x, void* codes, void* scal
 }
 
 }  // namespace lik
+
+// ---- dequantize to fp16 (prefill / materialize path) -----------------------
+// fp16(code * scale [+ zero]) exactly as the reference's dequantize helpers
+// compute it (fp32 product, one rounding to fp16; the asymmetric add happens in
+// fp32 before the rounding). One 16-lane half-warp per token row.
+
+namespace lik {
+namespace {
+
+// FMT: 0 = INT8 per token, 1 = INT4 KIVI symmetric, 2 = INT4 KIVI asymmetric.
+template <int FMT>
+__global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* __restrict__ kq, const __half* __restrict__ ks,
+                                                     const __half* __restrict__ kz, const uint8_t* __restrict__ vq,
+                                                     const __half* __restrict__ vs, const __half* __restrict__ vz,
+                                                     __half* __restrict__ kout, __half* __restrict__ vout,
+                                                     long long n_rows, long long seqlen, long long buf, int gs,
+                                                     long long ng_buf) {
+    const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 4;
+    if (row >= n_rows) return;
+    const int l = threadIdx.x & 15;  // channels 8l .. 8l+7
+    const long long slab = row / seqlen;
+    const long long t = row - slab * seqlen;
+    const long long src = slab * buf + t;
+    float k[8], v[8];
+    if (FMT == 0) {
+        const uint2 a = reinterpret_cast<const uint2*>(kq + src * kHeadDim)[l];
+        const uint2 b = reinterpret_cast<const uint2*>(vq + src * kHeadDim)[l];
+        const float sk = __half2float(ks[src]), sv = __half2float(vs[src]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            k[i] = static_cast<float>(static_cast<int8_t>(a.x >> (8 * i))) * sk;
+            k[4 + i] = static_cast<float>(static_cast<int8_t>(a.y >> (8 * i))) * sk;
+            v[i] = static_cast<float>(static_cast<int8_t>(b.x >> (8 * i))) * sv;
+            v[4 + i] = static_cast<float>(static_cast<int8_t>(b.y >> (8 * i))) * sv;
+        }
+    } else {
+        const uint32_t a = reinterpret_cast<const uint32_t*>(kq + src * (kHeadDim / 2))[l];
+        const uint32_t b = reinterpret_cast<const uint32_t*>(vq + src * (kHeadDim / 2))[l];
+        const long long g = slab * ng_buf + t / gs;
+        const float sv = __half2float(vs[src]);
+        const float zv = FMT == 2 ? __half2float(vz[src]) : 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            int ck = (a >> (4 * i)) & 0xF, cv = (b >> (4 * i)) & 0xF;
+            if (FMT == 1) {
+                ck = ck >= 8 ? ck - 16 : ck;
+                cv = cv >= 8 ? cv - 16 : cv;
+            }
+            const int ch = 8 * l + i;
+            const float sk = __half2float(ks[g * kHeadDim + ch]);
+            if (FMT == 2) {
+                const float zk = __half2float(kz[g * kHeadDim + ch]);
+                k[i] = __fadd_rn(__fmul_rn(static_cast<float>(ck), sk), zk);
+                v[i] = __fadd_rn(__fmul_rn(static_cast<float>(cv), sv), zv);
+            } else {
+                k[i] = static_cast<float>(ck) * sk;
+                v[i] = static_cast<float>(cv) * sv;
+            }
+        }
+    }
+    uint4 ko, vo;
+    __half* kh = reinterpret_cast<__half*>(&ko);
+    __half* vh = reinterpret_cast<__half*>(&vo);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        kh[i] = __float2half_rn(k[i]);
+        vh[i] = __float2half_rn(v[i]);
+    }
+    reinterpret_cast<uint4*>(kout + row * kHeadDim)[l] = ko;
+    reinterpret_cast<uint4*>(vout + row * kHeadDim)[l] = vo;
+}
+
+}  // namespace
+
+lik_status launch_dequant(int fmt, const void* kq, const void* ks, const void* kz, const void* vq, const void* vs,
+                          const void* vz, void* kout, void* vout, int64_t n_slabs, int64_t seqlen,
+                          int64_t kv_buf_len, int64_t group_size, int64_t n_groups_buf, cudaStream_t stream,
+                          std::string& err) {
+    const long long n_rows = static_cast<long long>(n_slabs) * seqlen;
+    if (n_rows == 0) return LIK_OK;
+    const long long blocks = (n_rows + 15) / 16;
+    if (blocks > 0x7fffffffLL) {
+        err = "too many rows";
+        return LIK_ERR_INVALID_ARGUMENT;
+    }
+    auto c = [](const void* p) { return static_cast<const uint8_t*>(p); };
+    auto h = [](const void* p) { return static_cast<const __half*>(p); };
+    __half* ko = static_cast<__half*>(kout);
+    __half* vo = static_cast<__half*>(vout);
+    const int gs = static_cast<int>(group_size > 0 ? group_size : 1);
+    const unsigned nb = static_cast<unsigned>(blocks);
+    if (fmt == 0)
+        dequant_kernel<0><<<nb, 256, 0, stream>>>(c(kq), h(ks), h(kz), c(vq), h(vs), h(vz), ko, vo, n_rows, seqlen,
+                                                 kv_buf_len, gs, n_groups_buf);
+    else if (fmt == 1)
+        dequant_kernel<1><<<nb, 256, 0, stream>>>(c(kq), h(ks), h(kz), c(vq), h(vs), h(vz), ko, vo, n_rows, seqlen,
+                                                 kv_buf_len, gs, n_groups_buf);
+    else
+        dequant_kernel<2><<<nb, 256, 0, stream>>>(c(kq), h(ks), h(kz), c(vq), h(vs), h(vz), ko, vo, n_rows, seqlen,
+                                                 kv_buf_len, gs, n_groups_buf);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        err = std::string("dequantize launch: ") + cudaGetErrorString(e);
+        return LIK_ERR_CUDA;
+    }
+    return LIK_OK;
+}
+
+}  // namespace lik

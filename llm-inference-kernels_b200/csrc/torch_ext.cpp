@@ -342,6 +342,61 @@ void quantize_k_per_channel_groupwise_int4_into(torch::Tensor x, torch::Tensor c
     ok_or_throw(st, "quantize_k_per_channel_groupwise_int4_into");
 }
 
+// ---------------------------------------------------------------- dequantize
+
+std::tuple<torch::Tensor, torch::Tensor> dequant_out(const torch::Tensor& codes, int64_t s) {
+    auto o = codes.options().dtype(torch::kHalf);
+    return {torch::empty({codes.size(0), codes.size(1), s, 128}, o),
+            torch::empty({codes.size(0), codes.size(1), s, 128}, o)};
+}
+
+std::tuple<torch::Tensor, torch::Tensor> dequantize_int8(torch::Tensor k_q, torch::Tensor k_scale, torch::Tensor v_q,
+                                                         torch::Tensor v_scale, int64_t seqlen) {
+    check_kv4(k_q, "k_q", torch::kInt8, 128);
+    check_kv4(v_q, "v_q", torch::kInt8, 128);
+    TORCH_CHECK(k_q.sizes() == v_q.sizes(), "k_q and v_q must have the same shape");
+    check_tok_scale(k_scale, k_q, "k_scale");
+    check_tok_scale(v_scale, v_q, "v_scale");
+    const c10::cuda::CUDAGuard guard(k_q.device());
+    const int64_t s = live_len(seqlen, k_q.size(2));
+    auto [ko, vo] = dequant_out(k_q, s);
+    ok_or_throw(lik_dequantize_int8(k_q.data_ptr<int8_t>(), k_scale.data_ptr(), v_q.data_ptr<int8_t>(),
+                                    v_scale.data_ptr(), ko.data_ptr(), vo.data_ptr(), k_q.size(0), k_q.size(1), s,
+                                    k_q.size(2), 128, cur_stream()),
+                "dequantize_int8");
+    return {ko, vo};
+}
+
+std::tuple<torch::Tensor, torch::Tensor> dequantize_int4(torch::Tensor k_q, torch::Tensor k_scale, torch::Tensor v_q,
+                                                         torch::Tensor v_scale, int64_t group_size, int64_t seqlen,
+                                                         c10::optional<torch::Tensor> k_zero,
+                                                         c10::optional<torch::Tensor> v_zero) {
+    check_kv4(k_q, "k_q", torch::kInt8, 64);
+    check_kv4(v_q, "v_q", torch::kInt8, 64);
+    TORCH_CHECK(k_q.sizes() == v_q.sizes(), "k_q and v_q must have the same shape");
+    check_group_scale(k_scale, k_q, "k_scale");
+    check_tok_scale(v_scale, v_q, "v_scale");
+    TORCH_CHECK(k_zero.has_value() == v_zero.has_value(), "give both zero points or neither");
+    const c10::cuda::CUDAGuard guard(k_q.device());
+    const int64_t s = live_len(seqlen, k_q.size(2));
+    auto [ko, vo] = dequant_out(k_q, s);
+    lik_status st;
+    if (k_zero.has_value()) {
+        check_group_scale(*k_zero, k_q, "k_zero");
+        check_tok_scale(*v_zero, v_q, "v_zero");
+        st = lik_dequantize_int4_asym(k_q.data_ptr<int8_t>(), k_scale.data_ptr(), k_zero->data_ptr(),
+                                      v_q.data_ptr<int8_t>(), v_scale.data_ptr(), v_zero->data_ptr(), ko.data_ptr(),
+                                      vo.data_ptr(), k_q.size(0), k_q.size(1), s, k_q.size(2), 128, group_size,
+                                      k_scale.size(2), cur_stream());
+    } else {
+        st = lik_dequantize_int4(k_q.data_ptr<int8_t>(), k_scale.data_ptr(), v_q.data_ptr<int8_t>(),
+                                 v_scale.data_ptr(), ko.data_ptr(), vo.data_ptr(), k_q.size(0), k_q.size(1), s,
+                                 k_q.size(2), 128, group_size, k_scale.size(2), cur_stream());
+    }
+    ok_or_throw(st, "dequantize_int4");
+    return {ko, vo};
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -383,4 +438,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           "(a multiple of group_size)",
           py::arg("x"), py::arg("codes"), py::arg("scale"), py::arg("group_size"), py::arg("pos"),
           py::arg("zero") = py::none());
+    m.def("dequantize_int8", &dequantize_int8, "INT8 per-token KV -> fp16 K, V (first seqlen positions)",
+          py::arg("k_q"), py::arg("k_scale"), py::arg("v_q"), py::arg("v_scale"), py::arg("seqlen") = -1);
+    m.def("dequantize_int4", &dequantize_int4,
+          "INT4 KIVI KV -> fp16 K, V (zero points given: asymmetric format)", py::arg("k_q"), py::arg("k_scale"),
+          py::arg("v_q"), py::arg("v_scale"), py::arg("group_size"), py::arg("seqlen") = -1,
+          py::arg("k_zero") = py::none(), py::arg("v_zero") = py::none());
 }
