@@ -76,6 +76,13 @@ lik_status lik_workspace_init(void* workspace, size_t workspace_bytes, void* str
 lik_status lik_workspace_check(void* workspace, size_t workspace_bytes, void* stream,
                                int* device_error);
 
+/* Failure-detection self test (no reference counterpart): runs a one-warp
+ * kernel that waits, with the decode kernels' bounded poll loop limited to
+ * `polls` polls, on a shared-memory barrier nothing arrives at. The wait must
+ * give up and report: returns LIK_ERR_DEVICE_TIMEOUT with *device_error = 1
+ * (synchronizes `stream`); the CUDA context stays usable. */
+lik_status lik_selftest_bounded_wait(int64_t polls, int* device_error, void* stream);
+
 /* ---- decode attention (single query token per sequence) -------------- */
 
 /* fp16 KV. Replaces launch_decode_attention_splitk

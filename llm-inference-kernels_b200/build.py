@@ -35,6 +35,7 @@ CU_SOURCES = {
     "quantize.cu": ["-fmad=false"],   # bit-exact quantization: no contraction
     "cabi.cu": [],
     "noalloc.cu": [],
+    "selftest.cu": [],
 }
 HEADERS = ["lik_device.cuh", "lik_internal.h"]
 

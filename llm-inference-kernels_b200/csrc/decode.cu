@@ -231,8 +231,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
     const int lane = tid & 31;
+    // per stage: "full" (q, K and its scales landed), "fullv" (V and its
+    // scales landed) and "empty" (all consumer warps are done with the stage)
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_bar);
-    uint64_t* empty = full + p.nst;
+    uint64_t* fullv = full + p.nst;
+    uint64_t* empty = fullv + p.nst;
     volatile int* misc = reinterpret_cast<volatile int*>(smem + p.off_misc);
 
     const long long cta = blockIdx.x;
@@ -242,6 +245,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
     if (tid == 0) {
         for (int s = 0; s < p.nst; ++s) {
             mbar_init(&full[s], 32);
+            mbar_init(&fullv[s], 32);
             mbar_init(&empty[s], kNCW);
         }
         misc[0] = 0;
@@ -294,18 +298,21 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
             }
             const bool new_unit = (j == 0 || ti == 0);
             if (lane == 0) {
-                uint32_t bytes = 2u * ntok * ROWB + (new_unit ? HB * kHeadDim * 2 : 0);
+                uint32_t bytes_k = ntok * ROWB + (new_unit ? HB * kHeadDim * 2 : 0);
+                uint32_t bytes_v = ntok * ROWB;
                 int g0 = 0, ngrp = 0;
                 if ((F::TOKK || F::TOKV) && p.tok_bulk) {
-                    bytes += (F::TOKK + F::TOKV + F::ZV) * n8 * 2;
+                    bytes_k += F::TOKK * n8 * 2;
+                    bytes_v += (F::TOKV + F::ZV) * n8 * 2;
                 }
                 if (F::KG && p.kg_smem) {
                     g0 = static_cast<int>(t0) / p.group_size;
                     const int g1 = (static_cast<int>(t0) + ntok - 1) / p.group_size;
                     ngrp = g1 - g0 + 1;
-                    bytes += (F::ZK ? 2 : 1) * ngrp * kHeadDim * 2;
+                    bytes_k += (F::ZK ? 2 : 1) * ngrp * kHeadDim * 2;
                 }
-                mbar_arrive_expect_tx(&full[st], bytes);
+                // K side first: QK can start while V is still in flight
+                mbar_arrive_expect_tx(&full[st], bytes_k);
                 if (new_unit) {
                     const int hb = static_cast<int>(unit - bk * p.nhb);
                     const long long b = bk / p.n_kv_heads;
@@ -314,19 +321,21 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                     bulk_g2s(sb + p.off_q, p.q + qo, HB * kHeadDim * 2, &full[st], pol);
                 }
                 bulk_g2s(sb, p.k + rowbase * ROWB, ntok * ROWB, &full[st], pol);
-                bulk_g2s(sb + p.off_v, p.v + rowbase * ROWB, ntok * ROWB, &full[st], pol);
-                if ((F::TOKK || F::TOKV) && p.tok_bulk) {
-                    if (F::TOKK) bulk_g2s(sb + p.off_ks, p.ks + rowbase, n8 * 2, &full[st], pol);
-                    if (F::TOKV) bulk_g2s(sb + p.off_vs, p.vs + rowbase, n8 * 2, &full[st], pol);
-                    if (F::ZV) bulk_g2s(sb + p.off_vz, p.vz + rowbase, n8 * 2, &full[st], pol);
-                }
+                if (F::TOKK && p.tok_bulk) bulk_g2s(sb + p.off_ks, p.ks + rowbase, n8 * 2, &full[st], pol);
                 if (F::KG && p.kg_smem) {
                     const long long gb = (bk * p.ng_buf + g0) * kHeadDim;
                     bulk_g2s(sb + p.off_kgs, p.ks + gb, ngrp * kHeadDim * 2, &full[st], pol);
                     if (F::ZK) bulk_g2s(sb + p.off_kgz, p.kz + gb, ngrp * kHeadDim * 2, &full[st], pol);
                 }
+                mbar_arrive_expect_tx(&fullv[st], bytes_v);
+                bulk_g2s(sb + p.off_v, p.v + rowbase * ROWB, ntok * ROWB, &fullv[st], pol);
+                if (p.tok_bulk) {
+                    if (F::TOKV) bulk_g2s(sb + p.off_vs, p.vs + rowbase, n8 * 2, &fullv[st], pol);
+                    if (F::ZV) bulk_g2s(sb + p.off_vz, p.vz + rowbase, n8 * 2, &fullv[st], pol);
+                }
             } else {
                 mbar_arrive(&full[st]);
+                mbar_arrive(&fullv[st]);
             }
             if (++st == p.nst) {
                 st = 0;
@@ -343,6 +352,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
             const long long first = j > p.nst ? j - p.nst : 0;
             for (long long jj = first; jj < j; ++jj) {
                 mbar_wait_bounded(&full[jj % p.nst], static_cast<uint32_t>((jj / p.nst) & 1));
+                mbar_wait_bounded(&fullv[jj % p.nst], static_cast<uint32_t>((jj / p.nst) & 1));
             }
             if (lane == 0) atomicExch(p.err, kDevWaitTimeout);
         }
@@ -607,6 +617,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                 for (int c = 0; c < PVC; ++c) acc[h][c] *= al[h];
 
             // ---------------- PV ----------------
+            if (misc[0] || !mbar_wait_bounded(&fullv[st], ph)) {
+                aborted = true;
+                misc[0] = 1;
+                if (lane == 0) atomicExch(p.err, kDevWaitTimeout);
+            }
             // V dequantized to fp16 as the oracle does; acc += p(f16) * v(f16) in fp32.
             if (FMT == kF16 || FMT == kI8) {
                 auto pv_token = [&](int t) {
@@ -918,7 +933,7 @@ lik_status launch_t(const DecodeArgs& a, const DeviceInfo& di, cudaStream_t stre
     const int pbuf_bytes = static_cast<int>(align_up(static_cast<size_t>(kNCW) * (T / kNCW) * HB * 2, 16));
     const int abuf_bytes = kNCW * HB * kHeadDim * 4;
     const int work = pbuf_bytes + abuf_bytes;
-    const int fixed = work + kNCW * HB * 3 * 4 + 64 + 2 * 8 * 8;
+    const int fixed = work + kNCW * HB * 3 * 4 + 64 + 3 * 8 * 8;
     int nst = (di.max_smem_optin - fixed - 256) / p.stage_bytes;
     nst = std::min(nst, 8);
     if (nst < 2) {
@@ -938,7 +953,7 @@ lik_status launch_t(const DecodeArgs& a, const DeviceInfo& di, cudaStream_t stre
     o2 += 16;
     o2 = align_up(o2, 8);
     p.off_bar = static_cast<int>(o2);
-    o2 += 2 * nst * 8;
+    o2 += 3 * nst * 8;
     const size_t smem = o2;
 
     p.n_ctas = static_cast<int>(std::min<long long>(p.total_tiles, di.sm_count));

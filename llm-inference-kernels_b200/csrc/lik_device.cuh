@@ -56,8 +56,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Wait for phase `parity` of `bar` to complete, polling at most kMaxPolls
 // times. Returns false on timeout (the caller records the error and leaves).
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
-    for (uint32_t i = 0; i < kMaxPolls; ++i) {
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint32_t max_polls = kMaxPolls) {
+    for (uint32_t i = 0; i < max_polls; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
     }
     return false;

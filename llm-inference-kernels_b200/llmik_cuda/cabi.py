@@ -28,6 +28,7 @@ SIGNATURES = {
     "lik_decode_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "lik_workspace_init": (_int, [_p, _sz, _p]),
     "lik_workspace_check": (_int, [_p, _sz, _p, C.POINTER(_int)]),
+    "lik_selftest_bounded_wait": (_int, [_i64, C.POINTER(_int), _p]),
     "lik_decode_attention_f16": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _f, _p, _sz, _p]),
     "lik_decode_attention_f16_noalloc": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _f, _p]),
     "lik_decode_attention_int8": (_int, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _f,

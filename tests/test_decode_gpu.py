@@ -225,3 +225,18 @@ def test_workspace_shared_across_shapes(L):
         q, k, v = _inputs(b, 32, 8, s, seed=b * 1000 + s)
         out = L.decode_attention(q.cuda(), k.cuda(), v.cuda(), SCALE)
         assert_attn_close(out.cpu().numpy(), O.decode_attention(q.numpy(), k.numpy(), v.numpy(), SCALE))
+
+
+def test_bounded_wait_expires_into_an_error_status(L):
+    """A device wait that nothing will satisfy gives up after its poll limit,
+    the host reads the error, and the context keeps working."""
+    import ctypes
+    from llmik_cuda import cabi
+    lib = cabi.lib()
+    err = ctypes.c_int(-1)
+    st = lib.lik_selftest_bounded_wait(1000, ctypes.byref(err), torch.cuda.current_stream().cuda_stream)
+    assert st == 6 and err.value == 1
+    assert b"bounded" in lib.lik_last_error()
+    q, k, v = _inputs(1, 32, 8, 64, seed=0)
+    out = L.decode_attention(q.cuda(), k.cuda(), v.cuda(), SCALE)
+    assert_attn_close(out.cpu().numpy(), O.decode_attention(q.numpy(), k.numpy(), v.numpy(), SCALE))
