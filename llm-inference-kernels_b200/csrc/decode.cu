@@ -624,17 +624,21 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
             }
             // V dequantized to fp16 as the oracle does; acc += p(f16) * v(f16) in fp32.
             if (FMT == kF16 || FMT == kI8) {
+                // per-tile base pointers; the full-tile loop is unrolled so
+                // every per-position offset is an immediate
+                const uint8_t* vrow = sV + wt0 * ROWB + lane * (FMT == kF16 ? 8 : 4);
+                const __half* vsr = svs + wt0;
                 auto pv_token = [&](int t) {
                     uint32_t v0, v1;
                     if (FMT == kF16) {
-                        const uint2 vv = *reinterpret_cast<const uint2*>(sV + (wt0 + t) * ROWB + lane * 8);
+                        const uint2 vv = *reinterpret_cast<const uint2*>(vrow + t * ROWB);
                         v0 = vv.x;
                         v1 = vv.y;
                     } else {
-                        const uint32_t vv = *reinterpret_cast<const uint32_t*>(sV + (wt0 + t) * ROWB + lane * 4);
+                        const uint32_t vv = *reinterpret_cast<const uint32_t*>(vrow + t * ROWB);
                         half2 lo, hi;
                         i8x4_to_h2(vv, lo, hi);
-                        const half2 s2 = __half2half2(svs[wt0 + t]);
+                        const half2 s2 = __half2half2(vsr[t]);
                         v0 = as_u32(__hmul2(lo, s2));
                         v1 = as_u32(__hmul2(hi, s2));
                     }
@@ -644,22 +648,31 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                     pv_accum<HB, 2, PVC>(pw, vv2, acc);
                 };
                 if (nval == TW) {
-#pragma unroll 4
-                    for (int t = 0; t < TW; ++t) pv_token(t);
+                    constexpr int U = TW <= 16 ? TW : 8;
+#pragma unroll 1
+                    for (int t0u = 0; t0u < TW; t0u += U) {
+#pragma unroll
+                        for (int t = 0; t < U; ++t) pv_token(t0u + t);
+                    }
                 } else {
                     for (int t = 0; t < nval; ++t) pv_token(t);
                 }
             } else {
                 const int hw = lane >> 4;
                 const int l16 = lane & 15;
-                auto pv_token = [&](int t) {
-                    const uint32_t vv = *reinterpret_cast<const uint32_t*>(sV + (wt0 + t) * ROWB + l16 * 4);
+                const uint8_t* vrow = sV + (wt0 + hw) * ROWB + l16 * 4;
+                const __half* vsr = svs + wt0 + hw;
+                const __half* vzr = svz + wt0 + hw;
+                const uint16_t* prow = pbuf + hw * HB;
+                // u = position offset relative to this half-warp's first position
+                auto pv_token = [&](int u) {
+                    const uint32_t vv = *reinterpret_cast<const uint32_t*>(vrow + u * ROWB);
                     half2 o[4];
                     i4x8_to_h2<F::SIGNED>(vv, o);
-                    const half2 s2 = __half2half2(svs[wt0 + t]);
+                    const half2 s2 = __half2half2(vsr[u]);
                     uint32_t vd[4];
                     if (F::ZV) {
-                        const half2 z2 = __half2half2(svz[wt0 + t]);
+                        const half2 z2 = __half2half2(vzr[u]);
 #pragma unroll
                         for (int k = 0; k < 4; ++k) vd[k] = as_u32(__hfma2(o[k], s2, z2));
                     } else {
@@ -667,14 +680,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                         for (int k = 0; k < 4; ++k) vd[k] = as_u32(__hmul2(o[k], s2));
                     }
                     uint32_t pw[(HB + 1) / 2];
-                    load_pw<HB>(pbuf + t * HB, pw);
+                    load_pw<HB>(prow + u * HB, pw);
                     pv_accum<HB, 4, PVC>(pw, vd, acc);
                 };
                 if (nval == TW) {
-#pragma unroll 4
-                    for (int t2 = 0; t2 < TW; t2 += 2) pv_token(t2 + hw);
+#pragma unroll 8
+                    for (int u = 0; u < TW; u += 2) pv_token(u);
                 } else {
-                    for (int t = hw; t < nval; t += 2) pv_token(t);
+                    for (int u = 0; u + hw < nval; u += 2) pv_token(u);
                 }
             }
             __syncwarp();
