@@ -539,7 +539,7 @@ def run_ours(args):
     }
     if rank == 0 and world == 1 and not args.no_cpu:
         med, _, cores = cpu_unit_sample(5, 1)
-        n = max(5, min(4000, int(15.0 / max(med, 1e-4))))
+        n = max(5, min(20000, int(15.0 / max(med, 1e-4))))
         med, total, cores = cpu_unit_sample(n, 1)
         line["cpu_baseline"] = {"value": unit_bytes_c1() / med / 1e12, "unit": "TB/s", "cores": cores,
                                 "kind": "port", "seconds": total,
