@@ -150,6 +150,27 @@ lik_status lik_decode_attention_int4_asym(
     int64_t seqlen, int64_t kv_buf_len, int64_t group_size, int64_t n_groups_buf,
     float softmax_scale, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Paged KV (block tables; vLLM-style layout, no reference counterpart: the
+ * reference has only contiguous caches). kv_format: 0 fp16, 1 INT8 per token,
+ * 2 INT4 KIVI symmetric, 3 INT4 KIVI asymmetric. Layouts:
+ *   k_cache, v_cache  [num_blocks, n_kv_heads, block_size, 128 | 64]
+ *   per-token scale / zero  [num_blocks, n_kv_heads, block_size]
+ *   K group scale / zero    [num_blocks, n_kv_heads, block_size / group_size, 128]
+ *   block_tables int32 [batch, max_blocks_per_seq]; context_lens int32 [batch]
+ * Sequence b attends over its first context_lens[b] positions (clamped to
+ * [0, max_context_len]; each must be >= 1); position t lives at row t %
+ * block_size of block block_tables[b][t / block_size]. block_size is a
+ * multiple of 16 (and of group_size for INT4); scale/zero pointers are
+ * 16-byte aligned. Same workspace rules as the contiguous entry points. */
+lik_status lik_decode_attention_paged(
+    int kv_format, const void* q, const void* k_cache, const void* v_cache,
+    const void* k_scale, const void* v_scale, const void* k_zero, const void* v_zero,
+    const int32_t* block_tables, const int32_t* context_lens, void* out,
+    int64_t batch, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim,
+    int64_t block_size, int64_t max_blocks_per_seq, int64_t max_context_len,
+    int64_t group_size, float softmax_scale,
+    void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- KV quantize / pack --------------------------------------------- */
 /*
  * Source x: [batch, n_kv_heads, n_tokens, head_dim] fp16, contiguous.

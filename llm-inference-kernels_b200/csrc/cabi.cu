@@ -353,4 +353,45 @@ lik_status lik_dequantize_int4_asym(const int8_t* k_q, const void* k_scale, cons
                           kv_buf_len, head_dim, group_size, n_groups_buf, stream);
 }
 
+lik_status lik_decode_attention_paged(int kv_format, const void* q, const void* k_cache, const void* v_cache,
+                                      const void* k_scale, const void* v_scale, const void* k_zero, const void* v_zero,
+                                      const int32_t* block_tables, const int32_t* context_lens, void* out,
+                                      int64_t batch, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim,
+                                      int64_t block_size, int64_t max_blocks_per_seq, int64_t max_context_len,
+                                      int64_t group_size, float softmax_scale, void* workspace,
+                                      size_t workspace_bytes, void* stream) {
+    lik_status s = check_heads(batch, n_heads, n_kv_heads, head_dim);
+    if (s != LIK_OK) return s;
+    if (kv_format < kF16 || kv_format > kI4Asym) return fail(LIK_ERR_INVALID_ARGUMENT, "unknown kv_format");
+    if (block_size <= 0 || block_size % 16 != 0 || block_size > (1 << 20))
+        return fail(LIK_ERR_INVALID_ARGUMENT, "block_size must be a positive multiple of 16");
+    if (max_blocks_per_seq <= 0 || max_context_len < 1 || max_context_len > block_size * max_blocks_per_seq ||
+        max_context_len > (int64_t{1} << 30))
+        return fail(LIK_ERR_INVALID_ARGUMENT, "need 1 <= max_context_len <= block_size * max_blocks_per_seq");
+    if (batch == 0) return LIK_OK;
+    if (!block_tables || !context_lens) return fail(LIK_ERR_INVALID_ARGUMENT, "null block table or lengths");
+    const bool quant = kv_format != kF16;
+    const bool int4 = kv_format == kI4Sym || kv_format == kI4Asym;
+    if (quant && (!k_scale || !v_scale)) return fail(LIK_ERR_INVALID_ARGUMENT, "null scale pointer");
+    if (kv_format == kI4Asym && (!k_zero || !v_zero)) return fail(LIK_ERR_INVALID_ARGUMENT, "null zero-point pointer");
+    if (quant && (!aligned16(k_scale) || !aligned16(v_scale) ||
+                  (kv_format == kI4Asym && (!aligned16(k_zero) || !aligned16(v_zero)))))
+        return fail(LIK_ERR_MISALIGNED, "scale / zero pointers must be 16-byte aligned");
+    if (int4 && (group_size <= 0 || block_size % group_size != 0))
+        return fail(LIK_ERR_INVALID_ARGUMENT, "group_size must divide block_size");
+    DecodeArgs a;
+    a.fmt = kv_format;
+    a.q = q; a.k = k_cache; a.v = v_cache; a.out = out;
+    a.k_scale = k_scale; a.v_scale = v_scale; a.k_zero = k_zero; a.v_zero = v_zero;
+    a.batch = batch; a.n_heads = n_heads; a.n_kv_heads = n_kv_heads;
+    a.seqlen = max_context_len; a.kv_buf_len = max_context_len;
+    a.group_size = int4 ? group_size : 0;
+    a.n_groups_buf = int4 ? (max_context_len + group_size - 1) / group_size : 0;
+    a.block_tables = block_tables; a.context_lens = context_lens;
+    a.block_size = block_size; a.max_blocks = max_blocks_per_seq;
+    a.softmax_scale = softmax_scale;
+    a.workspace = workspace; a.workspace_bytes = workspace_bytes;
+    return run_decode(a, stream);
+}
+
 }  // extern "C"

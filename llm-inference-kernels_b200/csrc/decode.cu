@@ -96,6 +96,13 @@ struct DecodeParams {
     int off_v, off_ks, off_vs, off_vz, off_kgs, off_kgz, off_q;
     int off_work, off_abuf, off_ml, off_misc, off_bar;
     float qscale;
+    // paged KV (paged != 0): caches are [num_blocks, n_kv_heads, block_size, row],
+    // per-token scales [num_blocks, n_kv_heads, block_size], K group scales
+    // [num_blocks, n_kv_heads, block_size / group_size, 128]; sequence b's
+    // position t lives in block block_tables[b * max_blocks + t / block_size].
+    const int* block_tables;
+    const int* ctx_lens;
+    int paged, block_size, max_blocks;
     float* part;
     unsigned* counters;
     int* err;
@@ -283,13 +290,20 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                 }
             }
             const long long t0 = ti * T;
-            const int ntok = static_cast<int>(min(static_cast<long long>(T), p.seqlen - t0));
+            const long long seq_b = bk / p.n_kv_heads;
+            const long long kvh_p = bk - seq_b * p.n_kv_heads;
+            long long len_b = p.seqlen;
+            if (p.paged) {
+                const long long cl = p.ctx_lens[seq_b];
+                len_b = cl < 0 ? 0 : (cl > p.seqlen ? p.seqlen : cl);
+            }
+            const int ntok = static_cast<int>(max(0LL, min(static_cast<long long>(T), len_b - t0)));
             const long long rowbase = bk * p.kv_buf_len + t0;
             uint8_t* sb = smem + static_cast<size_t>(st) * p.stage_bytes;
             const int n8 = (ntok + 7) & ~7;
 
             // Scales that cannot use a bulk copy (unaligned slabs): plain loads.
-            if ((F::TOKK || F::TOKV) && !p.tok_bulk) {
+            if ((F::TOKK || F::TOKV) && !p.tok_bulk && !p.paged) {
                 for (int t = lane; t < ntok; t += 32) {
                     if (F::TOKK) reinterpret_cast<__half*>(sb + p.off_ks)[t] = p.ks[rowbase + t];
                     if (F::TOKV) reinterpret_cast<__half*>(sb + p.off_vs)[t] = p.vs[rowbase + t];
@@ -297,7 +311,56 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                 }
             }
             const bool new_unit = (j == 0 || ti == 0);
-            if (lane == 0) {
+            if (lane == 0 && p.paged) {
+                // gather the tile block by block (one bulk copy per block touched)
+                const int bs = p.block_size;
+                const int* bt = p.block_tables + seq_b * p.max_blocks;
+                uint32_t bytes_k = new_unit ? HB * kHeadDim * 2 : 0, bytes_v = 0;
+                for (long long pos = t0; pos < t0 + ntok;) {
+                    const int off = static_cast<int>(pos % bs);
+                    const int n = static_cast<int>(min(static_cast<long long>(bs - off), t0 + ntok - pos));
+                    const int nn8 = (n + 7) & ~7;
+                    bytes_k += n * ROWB + (F::TOKK ? nn8 * 2 : 0);
+                    bytes_v += n * ROWB + (F::TOKV ? nn8 * 2 : 0) + (F::ZV ? nn8 * 2 : 0);
+                    if (F::KG && p.kg_smem)
+                        bytes_k += (F::ZK ? 2 : 1) * ((pos + n - 1) / p.group_size - pos / p.group_size + 1) *
+                                   kHeadDim * 2;
+                    pos += n;
+                }
+                mbar_arrive_expect_tx(&full[st], bytes_k);
+                mbar_arrive_expect_tx(&fullv[st], bytes_v);
+                if (new_unit) {
+                    const int hb = static_cast<int>(unit - bk * p.nhb);
+                    const long long qo = (seq_b * p.n_heads + kvh_p * p.nhb * HB + hb * HB) * kHeadDim;
+                    bulk_g2s(sb + p.off_q, p.q + qo, HB * kHeadDim * 2, &full[st], pol);
+                }
+                const long long g0 = F::KG ? t0 / p.group_size : 0;
+                for (long long pos = t0; pos < t0 + ntok;) {
+                    const int off = static_cast<int>(pos % bs);
+                    const int n = static_cast<int>(min(static_cast<long long>(bs - off), t0 + ntok - pos));
+                    const int nn8 = (n + 7) & ~7;
+                    const long long page = bt[pos / bs];
+                    const long long row = (page * p.n_kv_heads + kvh_p) * bs + off;
+                    const int d = static_cast<int>(pos - t0);
+                    bulk_g2s(sb + d * ROWB, p.k + row * ROWB, n * ROWB, &full[st], pol);
+                    bulk_g2s(sb + p.off_v + d * ROWB, p.v + row * ROWB, n * ROWB, &fullv[st], pol);
+                    if (F::TOKK) bulk_g2s(sb + p.off_ks + d * 2, p.ks + row, nn8 * 2, &full[st], pol);
+                    if (F::TOKV) bulk_g2s(sb + p.off_vs + d * 2, p.vs + row, nn8 * 2, &fullv[st], pol);
+                    if (F::ZV) bulk_g2s(sb + p.off_vz + d * 2, p.vz + row, nn8 * 2, &fullv[st], pol);
+                    if (F::KG && p.kg_smem) {
+                        const long long ga = pos / p.group_size, gb2 = (pos + n - 1) / p.group_size;
+                        const long long gsrc = ((page * p.n_kv_heads + kvh_p) * (bs / p.group_size) +
+                                                off / p.group_size) * kHeadDim;
+                        const int gcnt = static_cast<int>(gb2 - ga + 1);
+                        bulk_g2s(sb + p.off_kgs + (ga - g0) * kHeadDim * 2, p.ks + gsrc, gcnt * kHeadDim * 2,
+                                 &full[st], pol);
+                        if (F::ZK)
+                            bulk_g2s(sb + p.off_kgz + (ga - g0) * kHeadDim * 2, p.kz + gsrc, gcnt * kHeadDim * 2,
+                                     &full[st], pol);
+                    }
+                    pos += n;
+                }
+            } else if (lane == 0) {
                 uint32_t bytes_k = ntok * ROWB + (new_unit ? HB * kHeadDim * 2 : 0);
                 uint32_t bytes_v = ntok * ROWB;
                 int g0 = 0, ngrp = 0;
@@ -305,7 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                     bytes_k += F::TOKK * n8 * 2;
                     bytes_v += (F::TOKV + F::ZV) * n8 * 2;
                 }
-                if (F::KG && p.kg_smem) {
+                if (F::KG && p.kg_smem && ntok > 0) {
                     g0 = static_cast<int>(t0) / p.group_size;
                     const int g1 = (static_cast<int>(t0) + ntok - 1) / p.group_size;
                     ngrp = g1 - g0 + 1;
@@ -322,7 +385,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                 }
                 bulk_g2s(sb, p.k + rowbase * ROWB, ntok * ROWB, &full[st], pol);
                 if (F::TOKK && p.tok_bulk) bulk_g2s(sb + p.off_ks, p.ks + rowbase, n8 * 2, &full[st], pol);
-                if (F::KG && p.kg_smem) {
+                if (F::KG && p.kg_smem && ntok > 0) {
                     const long long gb = (bk * p.ng_buf + g0) * kHeadDim;
                     bulk_g2s(sb + p.off_kgs, p.ks + gb, ngrp * kHeadDim * 2, &full[st], pol);
                     if (F::ZK) bulk_g2s(sb + p.off_kgz, p.kz + gb, ngrp * kHeadDim * 2, &full[st], pol);
@@ -387,7 +450,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
     uint32_t qh[HB][8];  // q * softmax_scale * log2e as half2, in the format's pair order
     uint32_t kg[8];      // INT4: K group scale of the lane's 16 channels (pair order)
     uint32_t kgz[8];     // INT4 asym: K group zero
-    long long cur_unit = -1, seg_t0 = 0, qoff = 0, bk = 0;
+    long long cur_unit = -1, seg_t0 = 0, qoff = 0, bk = 0, seq_len = 0;
     int cur_g = -1;
     int gnext = 0;  // INT4: first position (within the unit) of the next K group
     bool aborted = false;
@@ -410,6 +473,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
             const long long b = bk / p.n_kv_heads;
             const int kvh = static_cast<int>(bk - b * p.n_kv_heads);
             qoff = (b * p.n_heads + static_cast<long long>(kvh) * p.nhb * HB + hb * HB) * kHeadDim;
+            seq_len = p.seqlen;
+            if (p.paged) {
+                const long long cl = p.ctx_lens[b];
+                seq_len = cl < 0 ? 0 : (cl > p.seqlen ? p.seqlen : cl);
+            }
             m_run = -INFINITY;
             l_run = 0.f;
 #pragma unroll
@@ -466,7 +534,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
         LIK_TL(tid == 0 && i == tb, 1);
 
         const long long t0 = ti * T;
-        const int ntok = static_cast<int>(min(static_cast<long long>(T), p.seqlen - t0));
+        const int ntok = static_cast<int>(max(0LL, min(static_cast<long long>(T), seq_len - t0)));
         const uint8_t* sb = smem + static_cast<size_t>(st) * p.stage_bytes;
         const int wt0 = w * TW;
 
@@ -523,7 +591,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                                     gsp = reinterpret_cast<const __half*>(sb + p.off_kgs) + (g - g0) * kHeadDim;
                                     if (F::ZK) gzp = reinterpret_cast<const __half*>(sb + p.off_kgz) + (g - g0) * kHeadDim;
                                 } else {
-                                    const long long gb = (bk * p.ng_buf + g) * kHeadDim;
+                                    long long gb = (bk * p.ng_buf + g) * kHeadDim;
+                                    if (p.paged) {
+                                        const long long pos = static_cast<long long>(g) * p.group_size;
+                                        const long long sq = bk / p.n_kv_heads;
+                                        const long long page = p.block_tables[sq * p.max_blocks + pos / p.block_size];
+                                        gb = ((page * p.n_kv_heads + (bk - sq * p.n_kv_heads)) *
+                                                  (p.block_size / p.group_size) + (pos % p.block_size) / p.group_size) *
+                                             kHeadDim;
+                                    }
                                     gsp = p.ks + gb;
                                     if (F::ZK) gzp = p.kz + gb;
                                 }
@@ -745,8 +821,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                     for (int ww = 0; ww < kNCW; ++ww) M[h] = fmaxf(M[h], mlb[(ww * HB + h) * 3]);
                     L[h] = 0.f;
 #pragma unroll
-                    for (int ww = 0; ww < kNCW; ++ww)
-                        L[h] = fmaf(mlb[(ww * HB + h) * 3 + 1], fast_exp2(mlb[(ww * HB + h) * 3] - M[h]), L[h]);
+                    if (M[h] != -INFINITY)  // a segment of a paged sequence can hold no position
+#pragma unroll
+                        for (int ww = 0; ww < kNCW; ++ww)
+                            L[h] = fmaf(mlb[(ww * HB + h) * 3 + 1], fast_exp2(mlb[(ww * HB + h) * 3] - M[h]), L[h]);
                 }
                 auto pick = [&](const float (&x)[HB], int h) {
                     float r = x[0];
@@ -759,6 +837,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                     const int h = o >> 7;
                     const float mh = pick(M, h);
                     float a = 0.f;
+                    if (mh == -INFINITY) return a;
 #pragma unroll
                     for (int ww = 0; ww < kNCW; ++ww)
                         a = fmaf(fast_exp2(mlb[(ww * HB + h) * 3] - mh), abuf[(ww * HB + h) * kHeadDim + (o & 127)], a);
@@ -829,8 +908,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
 #pragma unroll
                                 for (int k = 0; k < SB; ++k) {
                                     const float mn = fmaxf(mg, ms[k]);
-                                    const float fa = fast_exp2(mg - mn);
-                                    const float fb = fast_exp2(ms[k] - mn);
+                                    const float fa = mg == -INFINITY ? 0.f : fast_exp2(mg - mn);
+                                    const float fb = ms[k] == -INFINITY ? 0.f : fast_exp2(ms[k] - mn);
                                     lg = lg * fa + ls[k] * fb;
                                     ag = ag * fa + as[k] * fb;
                                     mg = mn;
@@ -909,6 +988,11 @@ lik_status launch_t(const DecodeArgs& a, const DeviceInfo& di, cudaStream_t stre
     p.tpu = (a.seqlen + T - 1) / T;
     p.total_tiles = p.n_units * p.tpu;
     p.group_size = static_cast<int>(F::KG ? a.group_size : 1);
+    p.paged = a.block_tables != nullptr ? 1 : 0;
+    p.block_tables = a.block_tables;
+    p.ctx_lens = a.context_lens;
+    p.block_size = static_cast<int>(a.block_size);
+    p.max_blocks = static_cast<int>(a.max_blocks);
     p.qscale = a.softmax_scale * kLog2e;
 
     // Per-token scales ride the bulk copy when every tile's scale run is
@@ -921,6 +1005,10 @@ lik_status launch_t(const DecodeArgs& a, const DeviceInfo& di, cudaStream_t stre
     if (F::ZV) tok_bulk = tok_bulk && al16(a.v_zero);
     p.tok_bulk = tok_bulk ? 1 : 0;
     bool kg_smem = F::KG && a.group_size >= 32 && al16(a.k_scale) && (!F::ZK || al16(a.k_zero));
+    if (p.paged) {
+        p.tok_bulk = 1;  // block_size % 16 == 0 and 16-byte aligned scales (checked by the caller)
+        kg_smem = kg_smem && (a.block_size % a.group_size == 0);
+    }
     p.kg_smem = kg_smem ? 1 : 0;
     p.ngt = kg_smem ? static_cast<int>(std::min<int64_t>(a.n_groups_buf, (T + a.group_size - 1) / a.group_size + 1)) : 0;
 

@@ -28,6 +28,10 @@ struct DecodeArgs {
     int64_t seqlen = 0, kv_buf_len = 0;
     int64_t group_size = 0, n_groups_buf = 0;
     float softmax_scale = 0.f;
+    // paged KV: seqlen is the maximum context length, kv_buf_len unused
+    const int* block_tables = nullptr;
+    const int* context_lens = nullptr;
+    int64_t block_size = 0, max_blocks = 0;
     void* workspace = nullptr;
     size_t workspace_bytes = 0;
 };

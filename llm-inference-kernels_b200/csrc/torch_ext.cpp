@@ -342,6 +342,60 @@ void quantize_k_per_channel_groupwise_int4_into(torch::Tensor x, torch::Tensor c
     ok_or_throw(st, "quantize_k_per_channel_groupwise_int4_into");
 }
 
+// ---------------------------------------------------------------- paged
+
+torch::Tensor paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                                     torch::Tensor block_tables, torch::Tensor context_lens, double softmax_scale,
+                                     int64_t max_context_len, c10::optional<torch::Tensor> k_scale,
+                                     c10::optional<torch::Tensor> v_scale, int64_t group_size,
+                                     c10::optional<torch::Tensor> k_zero, c10::optional<torch::Tensor> v_zero) {
+    check_q(q);
+    check_cuda(k_cache, "k_cache");
+    check_cuda(v_cache, "v_cache");
+    TORCH_CHECK(k_cache.sizes() == v_cache.sizes(), "k_cache and v_cache must have the same shape");
+    TORCH_CHECK(k_cache.dim() == 4, "caches must be [num_blocks, n_kv_heads, block_size, row]");
+    check_cuda(block_tables, "block_tables");
+    check_cuda(context_lens, "context_lens");
+    TORCH_CHECK(block_tables.scalar_type() == torch::kInt32 && block_tables.dim() == 2 &&
+                    block_tables.size(0) == q.size(0),
+                "block_tables must be int32 [batch, max_blocks_per_seq]");
+    TORCH_CHECK(context_lens.scalar_type() == torch::kInt32 && context_lens.dim() == 1 &&
+                    context_lens.size(0) == q.size(0),
+                "context_lens must be int32 [batch]");
+    const int64_t hkv = k_cache.size(1);
+    TORCH_CHECK(hkv > 0 && q.size(1) % hkv == 0, "n_heads must be a multiple of n_kv_heads");
+    int fmt;
+    if (k_cache.scalar_type() == torch::kHalf) {
+        TORCH_CHECK(k_cache.size(3) == 128, "fp16 cache rows must be 128 wide");
+        fmt = 0;
+    } else {
+        TORCH_CHECK(k_cache.scalar_type() == torch::kInt8, "caches must be fp16 or int8 codes");
+        TORCH_CHECK(k_scale.has_value() && v_scale.has_value(), "quantized caches need k_scale and v_scale");
+        if (k_cache.size(3) == 128) {
+            fmt = 1;
+        } else {
+            TORCH_CHECK(k_cache.size(3) == 64, "packed INT4 rows must be 64 bytes");
+            fmt = k_zero.has_value() ? 3 : 2;
+        }
+    }
+    for (auto* t : {&k_cache, &v_cache, &block_tables, &context_lens}) check_same_device(q, *t);
+    const c10::cuda::CUDAGuard guard(q.device());
+    auto out = torch::empty_like(q);
+    at::Tensor& ws = workspace(q, lik_decode_workspace_bytes(q.size(0), q.size(1), hkv));
+    auto ptr = [](const c10::optional<torch::Tensor>& t) -> const void* {
+        return t.has_value() ? t->data_ptr() : nullptr;
+    };
+    ok_or_throw(lik_decode_attention_paged(fmt, q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), ptr(k_scale),
+                                           ptr(v_scale), ptr(k_zero), ptr(v_zero),
+                                           block_tables.data_ptr<int32_t>(), context_lens.data_ptr<int32_t>(),
+                                           out.data_ptr(), q.size(0), q.size(1), hkv, 128, k_cache.size(2),
+                                           block_tables.size(1), max_context_len, group_size,
+                                           static_cast<float>(softmax_scale), ws.data_ptr(), ws.numel(),
+                                           cur_stream()),
+                "paged_decode_attention");
+    return out;
+}
+
 // ---------------------------------------------------------------- dequantize
 
 std::tuple<torch::Tensor, torch::Tensor> dequant_out(const torch::Tensor& codes, int64_t s) {
@@ -438,6 +492,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           "(a multiple of group_size)",
           py::arg("x"), py::arg("codes"), py::arg("scale"), py::arg("group_size"), py::arg("pos"),
           py::arg("zero") = py::none());
+    m.def("paged_decode_attention", &paged_decode_attention,
+          "Decode attention over a paged KV cache (block tables, per-sequence lengths); the format follows the "
+          "cache dtype (fp16, int8 codes, packed int4; zero points given: asymmetric INT4)",
+          py::arg("q"), py::arg("k_cache"), py::arg("v_cache"), py::arg("block_tables"), py::arg("context_lens"),
+          py::arg("softmax_scale"), py::arg("max_context_len"), py::arg("k_scale") = py::none(),
+          py::arg("v_scale") = py::none(), py::arg("group_size") = 0, py::arg("k_zero") = py::none(),
+          py::arg("v_zero") = py::none());
     m.def("dequantize_int8", &dequantize_int8, "INT8 per-token KV -> fp16 K, V (first seqlen positions)",
           py::arg("k_q"), py::arg("k_scale"), py::arg("v_q"), py::arg("v_scale"), py::arg("seqlen") = -1);
     m.def("dequantize_int4", &dequantize_int4,

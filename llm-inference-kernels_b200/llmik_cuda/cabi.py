@@ -44,6 +44,8 @@ SIGNATURES = {
     "lik_quantize_v_per_token_int4_asym": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _p]),
     "lik_quantize_k_per_channel_groupwise_int4_asym": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64,
                                                               _i64, _i64, _i64, _p]),
+    "lik_decode_attention_paged": (_int, [_int, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64,
+                                          _i64, _i64, _i64, _i64, _f, _p, _sz, _p]),
     "lik_dequantize_int8": (_int, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p]),
     "lik_dequantize_int4": (_int, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p]),
     "lik_dequantize_int4_asym": (_int, [_p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
