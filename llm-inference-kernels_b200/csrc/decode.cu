@@ -163,6 +163,19 @@ __device__ __forceinline__ long long cta_first_tile(long long c, long long total
     return c * total / nctas;
 }
 
+// One step of the log-sum-exp merge of unit segments (running m, l, a) with
+// segment (ms, ls, as), with explicit roundings (no contraction left to the
+// compiler); a segment with ms = -inf (no positions) is an exact identity.
+__device__ __forceinline__ void lse_fold(float& mg, float& lg, float& ag, float ms, float ls, float as) {
+    const float mn = fmaxf(mg, ms);
+    const float fa = mg == -INFINITY ? 0.f : fast_exp2(mg - mn);
+    const float fb = ms == -INFINITY ? 0.f : fast_exp2(ms - mn);
+    lg = fmaf(lg, fa, __fmul_rn(ls, fb));
+    ag = fmaf(ag, fa, __fmul_rn(as, fb));
+    mg = mn;
+}
+constexpr int kMergeBatch = 4;  // segments whose loads are issued together
+
 // The HB fp16 softmax weights of one position as (HB+1)/2 packed words.
 template <int HB>
 __device__ __forceinline__ void load_pw(const uint16_t* src, uint32_t (&pw)[(HB + 1) / 2]) {
@@ -255,8 +268,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
             mbar_init(&fullv[s], 32);
             mbar_init(&empty[s], kNCW);
         }
-        misc[0] = 0;
-        misc[1] = 0;
+        misc[0] = 0;  // abort
+        misc[1] = 0;  // merge ticket result
         fence_barrier_init();
     }
     __syncthreads();
@@ -804,6 +817,17 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                         make_float4(acc[h][1], acc[h][3], acc[h][5], acc[h][7]);
                 }
             }
+            // the segment's state now lives in shared memory; the next segment
+            // starts from zero (clearing here also frees the registers for the
+            // combine and merge below)
+            m_run = -INFINITY;
+            l_run = 0.f;
+#pragma unroll
+            for (int h = 0; h < HB; ++h)
+#pragma unroll
+                for (int c = 0; c < PVC; ++c) acc[h][c] = 0.f;
+            const bool final_seg = (i == te - 1);
+            const bool whole = (seg_t0 == 0 && ti == p.tpu - 1);
             named_bar_sync(1, nct);  // B
             LIK_TL(tid == 0 && i == te - 1, 5);
             // All consumer warps combine the eight warp states and write the
@@ -811,21 +835,33 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
             // ticket -- and, if this CTA completes the unit, the merge -- waits
             // on global memory: done by warp 0 mid-stream (the other warps go
             // on streaming) and by every warp on the CTA's last segment.
-            const bool final_seg = (i == te - 1);
             {
-                float M[HB], L[HB];
+                // Lane j of every warp (j = lane & 7; lanes 8..31 repeat
+                // lanes 0..7) holds consumer warp j's (m, l) of each head:
+                // the head maximum M, the warp weights exp2(m_j - M) and the
+                // sum L are reduced with shuffles, identically in every lane.
+                float M[HB], L[HB], fw[HB];
+                {
+                    const int wsrc = lane & 7;
 #pragma unroll
-                for (int h = 0; h < HB; ++h) {
-                    M[h] = -INFINITY;
-#pragma unroll
-                    for (int ww = 0; ww < kNCW; ++ww) M[h] = fmaxf(M[h], mlb[(ww * HB + h) * 3]);
-                    L[h] = 0.f;
-#pragma unroll
-                    if (M[h] != -INFINITY)  // a segment of a paged sequence can hold no position
-#pragma unroll
-                        for (int ww = 0; ww < kNCW; ++ww)
-                            L[h] = fmaf(mlb[(ww * HB + h) * 3 + 1], fast_exp2(mlb[(ww * HB + h) * 3] - M[h]), L[h]);
+                    for (int h = 0; h < HB; ++h) {
+                        const float mw = mlb[(wsrc * HB + h) * 3];
+                        const float lw = mlb[(wsrc * HB + h) * 3 + 1];
+                        float mx = fmaxf(mw, __shfl_xor_sync(kFull, mw, 1));
+                        mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 2));
+                        mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 4));
+                        // a segment of a paged sequence can hold no position (M = -inf)
+                        const float f = mx == -INFINITY ? 0.f : fast_exp2(mw - mx);
+                        float ls = __fmul_rn(lw, f);
+                        ls += __shfl_xor_sync(kFull, ls, 1);
+                        ls += __shfl_xor_sync(kFull, ls, 2);
+                        ls += __shfl_xor_sync(kFull, ls, 4);
+                        M[h] = mx;
+                        L[h] = ls;
+                        fw[h] = f;
+                    }
                 }
+                LIK_TL(tid == 0 && final_seg, 9);
                 auto pick = [&](const float (&x)[HB], int h) {
                     float r = x[0];
 #pragma unroll
@@ -833,17 +869,58 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                         if (h == hx) r = x[hx];
                     return r;
                 };
+                // sum over the consumer warps of weight * raw accumulator; the
+                // head o >> 7 is the same across a warp (o steps by the
+                // consumer thread count from tid), so the weights are shuffled in
                 auto combined = [&](int o) {
                     const int h = o >> 7;
-                    const float mh = pick(M, h);
-                    float a = 0.f;
-                    if (mh == -INFINITY) return a;
+                    const float fh = pick(fw, h);
+                    float x[kNCW];
 #pragma unroll
-                    for (int ww = 0; ww < kNCW; ++ww)
-                        a = fmaf(fast_exp2(mlb[(ww * HB + h) * 3] - mh), abuf[(ww * HB + h) * kHeadDim + (o & 127)], a);
+                    for (int ww = 0; ww < kNCW; ++ww) x[ww] = abuf[(ww * HB + h) * kHeadDim + (o & 127)];
+                    float a = 0.f;
+#pragma unroll
+                    for (int ww = 0; ww < kNCW; ++ww) a = fmaf(__shfl_sync(kFull, fh, ww), x[ww], a);
                     return a;
                 };
-                const bool whole = (seg_t0 == 0 && ti == p.tpu - 1);
+                // The merge of a split unit's segments: a log-sum-exp fold, in
+                // CTA order, over their partials in the workspace. Threads wl,
+                // wl + nw, ... each produce outputs; two outputs per pass so
+                // that all their loads are in flight together.
+                auto merge_out = [&](long long c_lo, int nseg, bool lo_first, int wl, int nw) {
+                    constexpr int SB = kMergeBatch;
+                    constexpr int HBK = HB * kHeadDim;
+                    for (int o0 = wl; o0 < HBK; o0 += 2 * nw) {
+                        float mg[2], lg[2], ag[2];
+#pragma unroll
+                        for (int r = 0; r < 2; ++r) mg[r] = -INFINITY, lg[r] = 0.f, ag[r] = 0.f;
+                        for (int s0 = 0; s0 < nseg; s0 += SB) {
+                            float ms[2][SB], ls[2][SB], as[2][SB];
+#pragma unroll
+                            for (int r = 0; r < 2; ++r) {
+                                const int o = o0 + r * nw;
+                                const int h = (o < HBK ? o : 0) >> 7;
+#pragma unroll
+                                for (int k = 0; k < SB; ++k) {
+                                    const long long c2 = c_lo + s0 + k;
+                                    const bool ok = s0 + k < nseg && o < HBK;
+                                    const float* q2 =
+                                        p.part + (2 * (ok ? c2 : c_lo) + ((ok && c2 == c_lo && !lo_first) ? 1 : 0)) * SL;
+                                    ms[r][k] = ok ? __ldcg(q2 + HBK + h) : -INFINITY;
+                                    ls[r][k] = ok ? __ldcg(q2 + HBK + HB + h) : 0.f;
+                                    as[r][k] = ok ? __ldcg(q2 + o) : 0.f;
+                                }
+                            }
+#pragma unroll
+                            for (int r = 0; r < 2; ++r)
+#pragma unroll
+                                for (int k = 0; k < SB; ++k) lse_fold(mg[r], lg[r], ag[r], ms[r][k], ls[r][k], as[r][k]);
+                        }
+#pragma unroll
+                        for (int r = 0; r < 2; ++r)
+                            if (o0 + r * nw < HBK) p.out[qoff + o0 + r * nw] = __float2half_rn(ag[r] / lg[r]);
+                    }
+                };
                 if (whole) {
                     for (int o = tid; o < HB * kHeadDim; o += nct)
                         p.out[qoff + o] = __float2half_rn(combined(o) / pick(L, o >> 7));
@@ -856,70 +933,40 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                         sp[HB * kHeadDim + HB + tid] = pick(L, tid);
                     }
                     named_bar_sync(1, nct);  // C: the whole partial is written
+                    LIK_TL(tid == 0 && final_seg, 10);
                 }
-            }
             LIK_TL(tid == 0 && i != te - 1 && seg_t0 != 0, 10);
-            const bool whole = (seg_t0 == 0 && ti == p.tpu - 1);
             if (!whole && (final_seg || w == 0)) {
                 const int wl = final_seg ? tid : lane;
                 const int nw = final_seg ? nct : 32;
-                {
-                    const long long c_lo = owner_cta(unit * p.tpu, p.total_tiles, p.n_ctas);
-                    const long long c_hi = owner_cta((unit + 1) * p.tpu - 1, p.total_tiles, p.n_ctas);
-                    int last = 0;
-                    if (wl == 0) {
-                        // release this CTA's partial / acquire the others' (cumulative
-                        // over barrier C)
-                        const unsigned old = atomic_add_acq_rel_gpu(&p.counters[unit], 1u);
-                        last = (old == static_cast<unsigned>(c_hi - c_lo));
-                        if (last) p.counters[unit] = 0u;
-                    }
-                    if (final_seg) {
-                        if (wl == 0) misc[1] = last;
-                        named_bar_sync(1, nct);
-                        last = misc[1];
-                    } else {
-                        last = __shfl_sync(kFull, last, 0);
-                        __syncwarp();
-                    }
-                    LIK_TL(tid == 0 && i == te - 1, 6);
-                    if (last) {
-                        // CTA c_lo's segment sits in its second slot unless its
-                        // range starts exactly at this unit's first tile; every
-                        // later CTA's segment is its first unit (slot 0).
-                        const bool lo_first = cta_first_tile(c_lo, p.total_tiles, p.n_ctas) == unit * p.tpu;
-                        const int nseg = static_cast<int>(c_hi - c_lo + 1);
-                        for (int o = wl; o < HB * kHeadDim; o += nw) {
-                            const int h = o >> 7;
-                            float mg = -INFINITY, lg = 0.f, ag = 0.f;
-                            constexpr int SB = 4;  // segments whose loads are issued together
-                            for (int s0 = 0; s0 < nseg; s0 += SB) {
-                                float ms[SB], ls[SB], as[SB];
-#pragma unroll
-                                for (int k = 0; k < SB; ++k) {
-                                    const long long c2 = c_lo + s0 + k;
-                                    const bool ok = s0 + k < nseg;
-                                    const float* q2 =
-                                        p.part + (2 * (ok ? c2 : c_lo) + ((ok && c2 == c_lo && !lo_first) ? 1 : 0)) * SL;
-                                    ms[k] = ok ? __ldcg(q2 + HB * kHeadDim + h) : -INFINITY;
-                                    ls[k] = ok ? __ldcg(q2 + HB * kHeadDim + HB + h) : 0.f;
-                                    as[k] = ok ? __ldcg(q2 + o) : 0.f;
-                                }
-#pragma unroll
-                                for (int k = 0; k < SB; ++k) {
-                                    const float mn = fmaxf(mg, ms[k]);
-                                    const float fa = mg == -INFINITY ? 0.f : fast_exp2(mg - mn);
-                                    const float fb = ms[k] == -INFINITY ? 0.f : fast_exp2(ms[k] - mn);
-                                    lg = lg * fa + ls[k] * fb;
-                                    ag = ag * fa + as[k] * fb;
-                                    mg = mn;
-                                }
-                            }
-                            p.out[qoff + o] = __float2half_rn(ag / lg);
-                        }
-                    }
+                const long long c_lo = owner_cta(unit * p.tpu, p.total_tiles, p.n_ctas);
+                const long long c_hi = owner_cta((unit + 1) * p.tpu - 1, p.total_tiles, p.n_ctas);
+                int last = 0;
+                if (wl == 0) {
+                    // release this CTA's partial / acquire the others' (cumulative
+                    // over barrier C)
+                    const unsigned old = atomic_add_acq_rel_gpu(&p.counters[unit], 1u);
+                    last = (old == static_cast<unsigned>(c_hi - c_lo));
+                    if (last) p.counters[unit] = 0u;
+                }
+                if (final_seg) {
+                    if (wl == 0) misc[1] = last;
+                    named_bar_sync(1, nct);
+                    last = misc[1];
+                } else {
+                    last = __shfl_sync(kFull, last, 0);
+                    __syncwarp();
+                }
+                LIK_TL(tid == 0 && i == te - 1, 6);
+                if (last) {
+                    // CTA c_lo's segment sits in its second slot unless its
+                    // range starts exactly at this unit's first tile; every
+                    // later CTA's segment is its first unit (slot 0).
+                    const bool lo_first = cta_first_tile(c_lo, p.total_tiles, p.n_ctas) == unit * p.tpu;
+                    merge_out(c_lo, static_cast<int>(c_hi - c_lo + 1), lo_first, wl, nw);
                 }
                 LIK_TL(tid == 0 && i == te - 1, 7);
+            }
             }
         }
         if (++st == p.nst) {
@@ -1051,7 +1098,7 @@ lik_status launch_t(const DecodeArgs& a, const DeviceInfo& di, cudaStream_t stre
     o2 += kNCW * HB * 3 * 4;
     o2 = align_up(o2, 16);
     p.off_misc = static_cast<int>(o2);
-    o2 += 16;
+    o2 += 32;
     o2 = align_up(o2, 8);
     p.off_bar = static_cast<int>(o2);
     o2 += 3 * nst * 8;
