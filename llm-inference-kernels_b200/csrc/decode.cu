@@ -53,7 +53,9 @@
 namespace lik {
 
 constexpr int kNCW = 8;                    // consumer warps
-constexpr int kThreads = (kNCW + 1) * 32;  // + producer warp
+constexpr int kProducerWarp = kNCW;      // issues the bulk copies
+constexpr int kEpilogueWarp = kNCW + 1;  // finishes unit segments off the streaming path
+constexpr int kThreads = (kNCW + 2) * 32;
 constexpr float kLog2e = 1.4426950408889634f;
 
 template <int FMT>
@@ -176,6 +178,126 @@ __device__ __forceinline__ void lse_fold(float& mg, float& lg, float& ag, float 
 }
 constexpr int kMergeBatch = 4;  // segments whose loads are issued together
 
+template <int HB>
+__device__ __forceinline__ float pick(const float (&x)[HB], int h) {
+    float r = x[0];
+#pragma unroll
+    for (int hx = 1; hx < HB; ++hx)
+        if (h == hx) r = x[hx];
+    return r;
+}
+
+// Combine of the eight consumer warps' raw states of one unit segment, read
+// from shared memory (mlb: m and l per (warp, head); abuf: 128 raw
+// accumulators per (warp, head)). Lane j of the calling warp (j = lane & 7;
+// lanes 8..31 repeat lanes 0..7) takes consumer warp j: the head maxima M, the
+// warp weights exp2(m_j - M) and the sums L are reduced with shuffles, with
+// the same result in every lane of every warp that runs it.
+template <int HB>
+struct WarpCombine {
+    float M[HB], L[HB], fw[HB];
+    __device__ __forceinline__ void load(const float* mlb, int lane) {
+        const int wsrc = lane & 7;
+#pragma unroll
+        for (int h = 0; h < HB; ++h) {
+            const float mw = mlb[(wsrc * HB + h) * 3];
+            const float lw = mlb[(wsrc * HB + h) * 3 + 1];
+            float mx = fmaxf(mw, __shfl_xor_sync(kFull, mw, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 2));
+            mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 4));
+            // a segment of a paged sequence can hold no position (M = -inf)
+            const float f = mx == -INFINITY ? 0.f : fast_exp2(mw - mx);
+            float ls = __fmul_rn(lw, f);
+            ls += __shfl_xor_sync(kFull, ls, 1);
+            ls += __shfl_xor_sync(kFull, ls, 2);
+            ls += __shfl_xor_sync(kFull, ls, 4);
+            M[h] = mx;
+            L[h] = ls;
+            fw[h] = f;
+        }
+    }
+    // sum over the consumer warps of weight * raw accumulator of output o
+    // (o >> 7 is the head; it must be the same across the calling warp)
+    __device__ __forceinline__ float combined(const float* abuf, int o) const {
+        const int h = o >> 7;
+        const float fh = pick<HB>(fw, h);
+        float x[kNCW];
+#pragma unroll
+        for (int ww = 0; ww < kNCW; ++ww) x[ww] = abuf[(ww * HB + h) * kHeadDim + (o & 127)];
+        float a = 0.f;
+#pragma unroll
+        for (int ww = 0; ww < kNCW; ++ww) a = fmaf(__shfl_sync(kFull, fh, ww), x[ww], a);
+        return a;
+    }
+};
+
+// Hand-off of a finished unit segment from the consumer warps to the
+// epilogue warp (shared memory, written by consumer warp 0 lane 0 before its
+// release-arrive on the hand-off barrier).
+struct EpiDesc {
+    long long unit, qoff, slot;
+    int whole, pad;
+};
+
+// The merge of a split unit's segments: a log-sum-exp fold, in CTA order,
+// over their partials in the workspace, normalised into `out`. Threads wl,
+// wl + nw, ... each produce outputs; two outputs per pass so that all their
+// loads are in flight together.
+template <int HB>
+__device__ __forceinline__ void merge_segments(const DecodeParams& p, long long unit, long long qoff, int wl, int nw) {
+    constexpr int SB = kMergeBatch;
+    constexpr int HBK = HB * kHeadDim;
+    constexpr int SL = HBK + 2 * HB;
+    const long long c_lo = owner_cta(unit * p.tpu, p.total_tiles, p.n_ctas);
+    const int nseg = static_cast<int>(owner_cta((unit + 1) * p.tpu - 1, p.total_tiles, p.n_ctas) - c_lo + 1);
+    // CTA c_lo's segment sits in its second slot unless its range starts
+    // exactly at this unit's first tile; every later CTA's segment is its
+    // first unit (slot 0).
+    const bool lo_first = cta_first_tile(c_lo, p.total_tiles, p.n_ctas) == unit * p.tpu;
+    for (int o0 = wl; o0 < HBK; o0 += 2 * nw) {
+        float mg[2], lg[2], ag[2];
+#pragma unroll
+        for (int r = 0; r < 2; ++r) mg[r] = -INFINITY, lg[r] = 0.f, ag[r] = 0.f;
+        for (int s0 = 0; s0 < nseg; s0 += SB) {
+            float ms[2][SB], ls[2][SB], as[2][SB];
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                const int o = o0 + r * nw;
+                const int h = (o < HBK ? o : 0) >> 7;
+#pragma unroll
+                for (int k = 0; k < SB; ++k) {
+                    const long long c2 = c_lo + s0 + k;
+                    const bool ok = s0 + k < nseg && o < HBK;
+                    const float* q2 = p.part + (2 * (ok ? c2 : c_lo) + ((ok && c2 == c_lo && !lo_first) ? 1 : 0)) * SL;
+                    ms[r][k] = ok ? __ldcg(q2 + HBK + h) : -INFINITY;
+                    ls[r][k] = ok ? __ldcg(q2 + HBK + HB + h) : 0.f;
+                    as[r][k] = ok ? __ldcg(q2 + o) : 0.f;
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < 2; ++r)
+#pragma unroll
+                for (int k = 0; k < SB; ++k) lse_fold(mg[r], lg[r], ag[r], ms[r][k], ls[r][k], as[r][k]);
+        }
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+            if (o0 + r * nw < HBK) p.out[qoff + o0 + r * nw] = __float2half_rn(ag[r] / lg[r]);
+    }
+}
+
+// Count this segment's partial towards its unit (acquire-release, GPU scope:
+// publishes the partial written before the call and, for the last arriver,
+// makes the other segments' partials visible). True when this segment
+// completes the unit; the counter is then reset for the next launch.
+__device__ __forceinline__ bool unit_ticket(const DecodeParams& p, long long unit) {
+    const long long c_lo = owner_cta(unit * p.tpu, p.total_tiles, p.n_ctas);
+    const long long c_hi = owner_cta((unit + 1) * p.tpu - 1, p.total_tiles, p.n_ctas);
+    const unsigned old = atomic_add_acq_rel_gpu(&p.counters[unit], 1u);
+    const bool last = old == static_cast<unsigned>(c_hi - c_lo);
+    if (last) p.counters[unit] = 0u;
+    return last;
+}
+
 // The HB fp16 softmax weights of one position as (HB+1)/2 packed words.
 template <int HB>
 __device__ __forceinline__ void load_pw(const uint16_t* src, uint32_t (&pw)[(HB + 1) / 2]) {
@@ -256,7 +378,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_bar);
     uint64_t* fullv = full + p.nst;
     uint64_t* empty = fullv + p.nst;
+    // segment hand-off to the epilogue warp: "epi_full" (the eight consumer
+    // warps wrote their state) and "epi_empty" (the epilogue warp has read it)
+    uint64_t* epi_full = empty + p.nst;
+    uint64_t* epi_empty = epi_full + 1;
     volatile int* misc = reinterpret_cast<volatile int*>(smem + p.off_misc);
+    EpiDesc* desc = reinterpret_cast<EpiDesc*>(smem + p.off_misc + 16);
+    float* abuf = reinterpret_cast<float*>(smem + p.off_abuf);
+    float* mlb = reinterpret_cast<float*>(smem + p.off_ml);
 
     const long long cta = blockIdx.x;
     const long long tb = cta_first_tile(cta, p.total_tiles, p.n_ctas);
@@ -268,6 +397,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
             mbar_init(&fullv[s], 32);
             mbar_init(&empty[s], kNCW);
         }
+        mbar_init(epi_full, kNCW);
+        mbar_init(epi_empty, 1);
         misc[0] = 0;  // abort
         misc[1] = 0;  // merge ticket result
         fence_barrier_init();
@@ -276,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
     LIK_TL(tid == 0, 0);
 
     // ======================= producer warp ================================
-    if (warp == kNCW) {
+    if (warp == kProducerWarp) {
         const uint64_t pol = l2_policy_evict_first();
         long long j = 0;
         bool ok = true;
@@ -435,6 +566,46 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
         return;
     }
 
+    // ======================= epilogue warp ================================
+    // Every unit segment but the CTA's last is finished here while the
+    // consumer warps go on streaming: combine the eight warp states, then
+    // either write the whole unit's output or publish this CTA's partial, take
+    // the unit's ticket and, if this segment completes the unit, merge it.
+    if (warp == kEpilogueWarp) {
+        constexpr int HBK = HB * kHeadDim;
+        const long long nhand = (te - 1) / p.tpu - tb / p.tpu;  // segment ends before the last
+        for (long long k = 0; k < nhand; ++k) {
+            if (!mbar_wait_bounded(epi_full, static_cast<uint32_t>(k & 1))) {
+                misc[0] = 1;
+                if (lane == 0) atomicExch(p.err, kDevWaitTimeout);
+                break;
+            }
+            const EpiDesc d = *desc;
+            WarpCombine<HB> wc;
+            wc.load(mlb, lane);
+            if (d.whole) {
+                for (int o = lane; o < HBK; o += 32)
+                    p.out[d.qoff + o] = __float2half_rn(wc.combined(abuf, o) / pick<HB>(wc.L, o >> 7));
+                __syncwarp();
+                if (lane == 0) mbar_arrive(epi_empty);
+            } else {
+                float* sp = p.part + d.slot * SL;
+                for (int o = lane; o < HBK; o += 32) sp[o] = wc.combined(abuf, o);
+                if (lane < HB) {
+                    sp[HBK + lane] = pick<HB>(wc.M, lane);
+                    sp[HBK + HB + lane] = pick<HB>(wc.L, lane);
+                }
+                __syncwarp();  // the partial is written; the shared state is free again
+                if (lane == 0) mbar_arrive(epi_empty);
+                int last = 0;
+                if (lane == 0) last = unit_ticket(p, d.unit);
+                last = __shfl_sync(kFull, last, 0);
+                if (last) merge_segments<HB>(p, d.unit, d.qoff, lane, 32);
+            }
+        }
+        return;
+    }
+
     // ======================= consumer warps ===============================
     const int w = warp;
     const int grp = lane >> 3;
@@ -454,9 +625,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
     const int nct = kNCW * 32;
 
     uint16_t* pbuf = reinterpret_cast<uint16_t*>(smem + p.off_work) + w * TW * HB;  // p as f16
-    float* abuf = reinterpret_cast<float*>(smem + p.off_abuf);
     const long long first_unit_of_cta = tb / p.tpu;
-    float* mlb = reinterpret_cast<float*>(smem + p.off_ml);
+    long long nhand = 0;  // segments handed to the epilogue warp so far
 
     float m_run = -INFINITY, l_run = 0.f;
     float acc[HB][PVC];
@@ -784,22 +954,28 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[st]);
 
-        // ---------------- end of a unit segment: merge and emit ----------------
-        // Every warp publishes its raw state; warp 0 alone combines the
-        // warps, writes the output (or a partial + ticket, and the cross-CTA
-        // merge when it completes the unit) while warps 1..7 go on streaming.
+        // ---------------- end of a unit segment ----------------
+        // Each warp stores its raw state (m, l, acc) in shared memory. A
+        // segment that is not the CTA's last is handed to the epilogue warp
+        // and the consumers go straight on to the next tile; the last one is
+        // finished here by all consumer warps together.
         if (ti == p.tpu - 1 || i == te - 1) {
-            LIK_TL(tid == 0 && i == te - 1, 4);
+            const bool final_seg = (i == te - 1);
+            const bool whole = (seg_t0 == 0 && ti == p.tpu - 1);
+            LIK_TL(tid == 0 && final_seg, 4);
             if (PVC == 8) {
 #pragma unroll
                 for (int h = 0; h < HB; ++h)
 #pragma unroll
                     for (int c = 0; c < 8; ++c) acc[h][c] += __shfl_xor_sync(kFull, acc[h][c], 16);
             }
-            LIK_TL(tid == 0 && i != te - 1 && seg_t0 != 0 && false == (i == te - 1), 9);
-            // A: warp 0 has finished the previous segment's combine (it reads
-            // abuf / mlb) before anyone overwrites them.
-            named_bar_sync(1, nct);
+            // the epilogue warp has read the previous hand-off
+            if (lane == 0 && nhand > 0 &&
+                !mbar_wait_bounded(epi_empty, static_cast<uint32_t>((nhand - 1) & 1))) {
+                misc[0] = 1;
+                atomicExch(p.err, kDevWaitTimeout);
+            }
+            __syncwarp();
             if (grp == 0 && prim && qpl == 0) {
                 mlb[(w * HB + hh) * 3] = m_run;
                 mlb[(w * HB + hh) * 3 + 1] = l_run;
@@ -818,155 +994,48 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                 }
             }
             // the segment's state now lives in shared memory; the next segment
-            // starts from zero (clearing here also frees the registers for the
-            // combine and merge below)
+            // starts from zero (clearing here also frees the registers)
             m_run = -INFINITY;
             l_run = 0.f;
 #pragma unroll
             for (int h = 0; h < HB; ++h)
 #pragma unroll
                 for (int c = 0; c < PVC; ++c) acc[h][c] = 0.f;
-            const bool final_seg = (i == te - 1);
-            const bool whole = (seg_t0 == 0 && ti == p.tpu - 1);
-            named_bar_sync(1, nct);  // B
-            LIK_TL(tid == 0 && i == te - 1, 5);
-            // All consumer warps combine the eight warp states and write the
-            // output (whole unit) or this CTA's partial. Only the completion
-            // ticket -- and, if this CTA completes the unit, the merge -- waits
-            // on global memory: done by warp 0 mid-stream (the other warps go
-            // on streaming) and by every warp on the CTA's last segment.
-            {
-                // Lane j of every warp (j = lane & 7; lanes 8..31 repeat
-                // lanes 0..7) holds consumer warp j's (m, l) of each head:
-                // the head maximum M, the warp weights exp2(m_j - M) and the
-                // sum L are reduced with shuffles, identically in every lane.
-                float M[HB], L[HB], fw[HB];
-                {
-                    const int wsrc = lane & 7;
-#pragma unroll
-                    for (int h = 0; h < HB; ++h) {
-                        const float mw = mlb[(wsrc * HB + h) * 3];
-                        const float lw = mlb[(wsrc * HB + h) * 3 + 1];
-                        float mx = fmaxf(mw, __shfl_xor_sync(kFull, mw, 1));
-                        mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 2));
-                        mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 4));
-                        // a segment of a paged sequence can hold no position (M = -inf)
-                        const float f = mx == -INFINITY ? 0.f : fast_exp2(mw - mx);
-                        float ls = __fmul_rn(lw, f);
-                        ls += __shfl_xor_sync(kFull, ls, 1);
-                        ls += __shfl_xor_sync(kFull, ls, 2);
-                        ls += __shfl_xor_sync(kFull, ls, 4);
-                        M[h] = mx;
-                        L[h] = ls;
-                        fw[h] = f;
-                    }
+            if (!final_seg) {
+                if (w == 0 && lane == 0) {
+                    EpiDesc d;
+                    d.unit = unit;
+                    d.qoff = qoff;
+                    d.slot = 2 * cta + (unit == first_unit_of_cta ? 0 : 1);
+                    d.whole = whole ? 1 : 0;
+                    d.pad = 0;
+                    *desc = d;
                 }
-                LIK_TL(tid == 0 && final_seg, 9);
-                auto pick = [&](const float (&x)[HB], int h) {
-                    float r = x[0];
-#pragma unroll
-                    for (int hx = 1; hx < HB; ++hx)
-                        if (h == hx) r = x[hx];
-                    return r;
-                };
-                // sum over the consumer warps of weight * raw accumulator; the
-                // head o >> 7 is the same across a warp (o steps by the
-                // consumer thread count from tid), so the weights are shuffled in
-                auto combined = [&](int o) {
-                    const int h = o >> 7;
-                    const float fh = pick(fw, h);
-                    float x[kNCW];
-#pragma unroll
-                    for (int ww = 0; ww < kNCW; ++ww) x[ww] = abuf[(ww * HB + h) * kHeadDim + (o & 127)];
-                    float a = 0.f;
-#pragma unroll
-                    for (int ww = 0; ww < kNCW; ++ww) a = fmaf(__shfl_sync(kFull, fh, ww), x[ww], a);
-                    return a;
-                };
-                // The merge of a split unit's segments: a log-sum-exp fold, in
-                // CTA order, over their partials in the workspace. Threads wl,
-                // wl + nw, ... each produce outputs; two outputs per pass so
-                // that all their loads are in flight together.
-                auto merge_out = [&](long long c_lo, int nseg, bool lo_first, int wl, int nw) {
-                    constexpr int SB = kMergeBatch;
-                    constexpr int HBK = HB * kHeadDim;
-                    for (int o0 = wl; o0 < HBK; o0 += 2 * nw) {
-                        float mg[2], lg[2], ag[2];
-#pragma unroll
-                        for (int r = 0; r < 2; ++r) mg[r] = -INFINITY, lg[r] = 0.f, ag[r] = 0.f;
-                        for (int s0 = 0; s0 < nseg; s0 += SB) {
-                            float ms[2][SB], ls[2][SB], as[2][SB];
-#pragma unroll
-                            for (int r = 0; r < 2; ++r) {
-                                const int o = o0 + r * nw;
-                                const int h = (o < HBK ? o : 0) >> 7;
-#pragma unroll
-                                for (int k = 0; k < SB; ++k) {
-                                    const long long c2 = c_lo + s0 + k;
-                                    const bool ok = s0 + k < nseg && o < HBK;
-                                    const float* q2 =
-                                        p.part + (2 * (ok ? c2 : c_lo) + ((ok && c2 == c_lo && !lo_first) ? 1 : 0)) * SL;
-                                    ms[r][k] = ok ? __ldcg(q2 + HBK + h) : -INFINITY;
-                                    ls[r][k] = ok ? __ldcg(q2 + HBK + HB + h) : 0.f;
-                                    as[r][k] = ok ? __ldcg(q2 + o) : 0.f;
-                                }
-                            }
-#pragma unroll
-                            for (int r = 0; r < 2; ++r)
-#pragma unroll
-                                for (int k = 0; k < SB; ++k) lse_fold(mg[r], lg[r], ag[r], ms[r][k], ls[r][k], as[r][k]);
-                        }
-#pragma unroll
-                        for (int r = 0; r < 2; ++r)
-                            if (o0 + r * nw < HBK) p.out[qoff + o0 + r * nw] = __float2half_rn(ag[r] / lg[r]);
-                    }
-                };
+                __syncwarp();
+                if (lane == 0) mbar_arrive(epi_full);  // release: the state and descriptor
+                ++nhand;
+            } else {
+                named_bar_sync(1, nct);  // every warp's state is in shared memory
+                LIK_TL(tid == 0, 5);
+                WarpCombine<HB> wc;
+                wc.load(mlb, lane);
                 if (whole) {
                     for (int o = tid; o < HB * kHeadDim; o += nct)
-                        p.out[qoff + o] = __float2half_rn(combined(o) / pick(L, o >> 7));
+                        p.out[qoff + o] = __float2half_rn(wc.combined(abuf, o) / pick<HB>(wc.L, o >> 7));
                 } else {
                     const long long slot = 2 * cta + (unit == first_unit_of_cta ? 0 : 1);
                     float* sp = p.part + slot * SL;
-                    for (int o = tid; o < HB * kHeadDim; o += nct) sp[o] = combined(o);
+                    for (int o = tid; o < HB * kHeadDim; o += nct) sp[o] = wc.combined(abuf, o);
                     if (tid < HB) {
-                        sp[HB * kHeadDim + tid] = pick(M, tid);
-                        sp[HB * kHeadDim + HB + tid] = pick(L, tid);
+                        sp[HB * kHeadDim + tid] = pick<HB>(wc.M, tid);
+                        sp[HB * kHeadDim + HB + tid] = pick<HB>(wc.L, tid);
                     }
-                    named_bar_sync(1, nct);  // C: the whole partial is written
-                    LIK_TL(tid == 0 && final_seg, 10);
-                }
-            LIK_TL(tid == 0 && i != te - 1 && seg_t0 != 0, 10);
-            if (!whole && (final_seg || w == 0)) {
-                const int wl = final_seg ? tid : lane;
-                const int nw = final_seg ? nct : 32;
-                const long long c_lo = owner_cta(unit * p.tpu, p.total_tiles, p.n_ctas);
-                const long long c_hi = owner_cta((unit + 1) * p.tpu - 1, p.total_tiles, p.n_ctas);
-                int last = 0;
-                if (wl == 0) {
-                    // release this CTA's partial / acquire the others' (cumulative
-                    // over barrier C)
-                    const unsigned old = atomic_add_acq_rel_gpu(&p.counters[unit], 1u);
-                    last = (old == static_cast<unsigned>(c_hi - c_lo));
-                    if (last) p.counters[unit] = 0u;
-                }
-                if (final_seg) {
-                    if (wl == 0) misc[1] = last;
+                    named_bar_sync(1, nct);  // the whole partial is written
+                    if (tid == 0) misc[1] = unit_ticket(p, unit) ? 1 : 0;
                     named_bar_sync(1, nct);
-                    last = misc[1];
-                } else {
-                    last = __shfl_sync(kFull, last, 0);
-                    __syncwarp();
+                    LIK_TL(tid == 0, 6);
+                    if (misc[1]) merge_segments<HB>(p, unit, qoff, tid, nct);
                 }
-                LIK_TL(tid == 0 && i == te - 1, 6);
-                if (last) {
-                    // CTA c_lo's segment sits in its second slot unless its
-                    // range starts exactly at this unit's first tile; every
-                    // later CTA's segment is its first unit (slot 0).
-                    const bool lo_first = cta_first_tile(c_lo, p.total_tiles, p.n_ctas) == unit * p.tpu;
-                    merge_out(c_lo, static_cast<int>(c_hi - c_lo + 1), lo_first, wl, nw);
-                }
-                LIK_TL(tid == 0 && i == te - 1, 7);
-            }
             }
         }
         if (++st == p.nst) {
@@ -1081,7 +1150,7 @@ lik_status launch_t(const DecodeArgs& a, const DeviceInfo& di, cudaStream_t stre
     const int pbuf_bytes = static_cast<int>(align_up(static_cast<size_t>(kNCW) * (T / kNCW) * HB * 2, 16));
     const int abuf_bytes = kNCW * HB * kHeadDim * 4;
     const int work = pbuf_bytes + abuf_bytes;
-    const int fixed = work + kNCW * HB * 3 * 4 + 64 + 3 * 8 * 8;
+    const int fixed = work + kNCW * HB * 3 * 4 + 80 + (3 * 8 + 2) * 8;
     int nst = (di.max_smem_optin - fixed - 256) / p.stage_bytes;
     nst = std::min(nst, 8);
     if (nst < 2) {
@@ -1098,10 +1167,10 @@ lik_status launch_t(const DecodeArgs& a, const DeviceInfo& di, cudaStream_t stre
     o2 += kNCW * HB * 3 * 4;
     o2 = align_up(o2, 16);
     p.off_misc = static_cast<int>(o2);
-    o2 += 32;
+    o2 += 16 + sizeof(EpiDesc);
     o2 = align_up(o2, 8);
     p.off_bar = static_cast<int>(o2);
-    o2 += 3 * nst * 8;
+    o2 += (3 * nst + 2) * 8;
     const size_t smem = o2;
 
     p.n_ctas = static_cast<int>(std::min<long long>(p.total_tiles, di.sm_count));
