@@ -403,6 +403,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
         misc[1] = 0;  // merge ticket result
         fence_barrier_init();
     }
+    // Programmatic dependent launch: this grid may start while the previous
+    // kernel on the stream is still finishing; nothing in global memory is
+    // read or written before that kernel has completed.
+    grid_dependency_wait();
     __syncthreads();
     LIK_TL(tid == 0, 0);
 
@@ -563,6 +567,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
             }
             if (lane == 0) atomicExch(p.err, kDevWaitTimeout);
         }
+        // Every copy is issued: the next kernel on the stream may be scheduled
+        // (it waits for this grid to complete before it touches memory).
+        // Measured on B200 with back-to-back steps: this early trigger saves
+        // about 1 us per INT8 / INT4 step and costs about 0.7 us per fp16
+        // step, so fp16 leaves the trigger to the CTA's exit.
+        if (FMT != kF16) grid_launch_dependents();
         return;
     }
 
@@ -1199,8 +1209,18 @@ lik_status launch_t(const DecodeArgs& a, const DeviceInfo& di, cudaStream_t stre
         err = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(attr_err[slot]);
         return LIK_ERR_CUDA;
     }
-    kern<<<p.n_ctas, kThreads, smem, stream>>>(p);
-    const cudaError_t e = cudaGetLastError();
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(p.n_ctas);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) {
         err = std::string("decode kernel launch: ") + cudaGetErrorString(e);
         return LIK_ERR_CUDA;

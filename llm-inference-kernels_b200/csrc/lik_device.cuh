@@ -93,6 +93,12 @@ __device__ __forceinline__ unsigned atomic_add_acq_rel_gpu(unsigned* p, unsigned
     return old;
 }
 
+// Programmatic dependent launch (sm_90+): wait until the grids this one
+// depends on have completed and their memory is visible / allow the next
+// grid on the stream to be scheduled.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
