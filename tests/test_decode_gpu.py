@@ -157,6 +157,40 @@ def test_repeated_calls_are_deterministic_and_workspace_self_cleans(L):
         assert torch.equal(o, outs[0])
 
 
+@pytest.mark.parametrize("fmt", ["f16", "int8", "int4", "int4_asym"])
+@pytest.mark.parametrize("b,s", [(128, 100), (64, 300), (40, 1)])
+def test_many_short_units_per_cta(L, fmt, b, s):
+    """Many short units: every CTA range holds several unit ends in
+    consecutive tiles (whole units and partial ones), so finished segments are
+    handed from the streaming warps to the finishing warp back to back. The
+    result must match the oracle and be identical on a repeated call."""
+    q, k, v = _inputs(b, 32, 8, s, seed=b * 7 + s, k_outliers=fmt.startswith("int4"))
+    qc, kc, vc = q.cuda(), k.cuda(), v.cuda()
+    if fmt == "f16":
+        run = lambda: L.decode_attention(qc, kc, vc, SCALE)
+        kd, vd = k.numpy(), v.numpy()
+    elif fmt == "int8":
+        kq, ks = L.quantize_per_token(kc)
+        vq, vs = L.quantize_per_token(vc)
+        run = lambda: L.decode_attention_int8(qc, kq, ks, vq, vs, SCALE)
+        kd, vd = O.dequant_int8_to_f16(kq.cpu().numpy(), ks.cpu().numpy(), vq.cpu().numpy(), vs.cpu().numpy())
+    elif fmt == "int4":
+        kq, ks = L.quantize_k_per_channel_groupwise_int4(kc, 32)
+        vq, vs = L.quantize_v_per_token_int4(vc)
+        run = lambda: L.decode_attention_int4(qc, kq, ks, vq, vs, 32, SCALE)
+        kd, vd = O.dequant_kivi_sym_to_f16(kq.cpu().numpy(), ks.cpu().numpy(), vq.cpu().numpy(),
+                                           vs.cpu().numpy(), 32)
+    else:
+        kq, ks, kz = L.quantize_k_per_channel_groupwise_int4_asym(kc, 32)
+        vq, vs, vz = L.quantize_v_per_token_int4_asym(vc)
+        run = lambda: L.decode_attention_int4_asym(qc, kq, ks, kz, vq, vs, vz, 32, SCALE)
+        kd, vd = O.dequant_kivi_asym_to_f16(kq.cpu().numpy(), ks.cpu().numpy(), kz.cpu().numpy(),
+                                            vq.cpu().numpy(), vs.cpu().numpy(), vz.cpu().numpy(), 32)
+    out = run()
+    assert_attn_close(out.cpu().numpy(), O.decode_attention(q.numpy(), kd, vd, SCALE))
+    assert torch.equal(run(), out)
+
+
 def test_64bit_offsets():
     """A cache whose byte offsets exceed 2^31 (K and V 2.4 GB each)."""
     import llmik_cuda as L
