@@ -243,17 +243,31 @@ struct EpiDesc {
 // over their partials in the workspace, normalised into `out`. Threads wl,
 // wl + nw, ... each produce outputs; two outputs per pass so that all their
 // loads are in flight together.
+// The CTAs whose ranges hold a unit: c_lo .. c_hi. CTA c_lo's segment sits
+// in its second partial slot unless its range starts exactly at the unit's
+// first tile (lo_first); every later CTA's segment is its first unit (slot 0).
+// (64-bit divisions: computed off the end-of-kernel critical path.)
+struct UnitSpan {
+    long long c_lo, c_hi;
+    bool lo_first;
+};
+__device__ __forceinline__ UnitSpan unit_span(const DecodeParams& p, long long unit) {
+    UnitSpan u;
+    u.c_lo = owner_cta(unit * p.tpu, p.total_tiles, p.n_ctas);
+    u.c_hi = owner_cta((unit + 1) * p.tpu - 1, p.total_tiles, p.n_ctas);
+    u.lo_first = cta_first_tile(u.c_lo, p.total_tiles, p.n_ctas) == unit * p.tpu;
+    return u;
+}
+
 template <int HB>
-__device__ __forceinline__ void merge_segments(const DecodeParams& p, long long unit, long long qoff, int wl, int nw) {
+__device__ __forceinline__ void merge_segments(const DecodeParams& p, const UnitSpan& sp, long long qoff, int wl,
+                                               int nw) {
     constexpr int SB = kMergeBatch;
     constexpr int HBK = HB * kHeadDim;
     constexpr int SL = HBK + 2 * HB;
-    const long long c_lo = owner_cta(unit * p.tpu, p.total_tiles, p.n_ctas);
-    const int nseg = static_cast<int>(owner_cta((unit + 1) * p.tpu - 1, p.total_tiles, p.n_ctas) - c_lo + 1);
-    // CTA c_lo's segment sits in its second slot unless its range starts
-    // exactly at this unit's first tile; every later CTA's segment is its
-    // first unit (slot 0).
-    const bool lo_first = cta_first_tile(c_lo, p.total_tiles, p.n_ctas) == unit * p.tpu;
+    const long long c_lo = sp.c_lo;
+    const int nseg = static_cast<int>(sp.c_hi - c_lo + 1);
+    const bool lo_first = sp.lo_first;
     for (int o0 = wl; o0 < HBK; o0 += 2 * nw) {
         float mg[2], lg[2], ag[2];
 #pragma unroll
@@ -289,11 +303,9 @@ __device__ __forceinline__ void merge_segments(const DecodeParams& p, long long 
 // publishes the partial written before the call and, for the last arriver,
 // makes the other segments' partials visible). True when this segment
 // completes the unit; the counter is then reset for the next launch.
-__device__ __forceinline__ bool unit_ticket(const DecodeParams& p, long long unit) {
-    const long long c_lo = owner_cta(unit * p.tpu, p.total_tiles, p.n_ctas);
-    const long long c_hi = owner_cta((unit + 1) * p.tpu - 1, p.total_tiles, p.n_ctas);
+__device__ __forceinline__ bool unit_ticket(const DecodeParams& p, long long unit, const UnitSpan& sp) {
     const unsigned old = atomic_add_acq_rel_gpu(&p.counters[unit], 1u);
-    const bool last = old == static_cast<unsigned>(c_hi - c_lo);
+    const bool last = old == static_cast<unsigned>(sp.c_hi - sp.c_lo);
     if (last) p.counters[unit] = 0u;
     return last;
 }
@@ -607,10 +619,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                 }
                 __syncwarp();  // the partial is written; the shared state is free again
                 if (lane == 0) mbar_arrive(epi_empty);
+                const UnitSpan span = unit_span(p, d.unit);
                 int last = 0;
-                if (lane == 0) last = unit_ticket(p, d.unit);
+                if (lane == 0) last = unit_ticket(p, d.unit, span);
                 last = __shfl_sync(kFull, last, 0);
-                if (last) merge_segments<HB>(p, d.unit, d.qoff, lane, 32);
+                if (last) merge_segments<HB>(p, span, d.qoff, lane, 32);
             }
         }
         return;
@@ -637,6 +650,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
     uint16_t* pbuf = reinterpret_cast<uint16_t*>(smem + p.off_work) + w * TW * HB;  // p as f16
     const long long first_unit_of_cta = tb / p.tpu;
     long long nhand = 0;  // segments handed to the epilogue warp so far
+    // span of the CTA's last unit, needed right after its final segment;
+    // computed now, while the first tiles are still in flight, and kept in
+    // shared memory (read after the final segment's barriers)
+    UnitSpan* last_span = reinterpret_cast<UnitSpan*>(smem + p.off_misc + 16 + sizeof(EpiDesc));
+    if (tid == 0) *last_span = unit_span(p, (te - 1) / p.tpu);
 
     float m_run = -INFINITY, l_run = 0.f;
     float acc[HB][PVC];
@@ -1041,10 +1059,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                         sp[HB * kHeadDim + HB + tid] = pick<HB>(wc.L, tid);
                     }
                     named_bar_sync(1, nct);  // the whole partial is written
-                    if (tid == 0) misc[1] = unit_ticket(p, unit) ? 1 : 0;
+                    if (tid == 0) misc[1] = unit_ticket(p, unit, *last_span) ? 1 : 0;
                     named_bar_sync(1, nct);
                     LIK_TL(tid == 0, 6);
-                    if (misc[1]) merge_segments<HB>(p, unit, qoff, tid, nct);
+                    if (misc[1]) merge_segments<HB>(p, *last_span, qoff, tid, nct);
                 }
             }
         }
@@ -1177,7 +1195,7 @@ lik_status launch_t(const DecodeArgs& a, const DeviceInfo& di, cudaStream_t stre
     o2 += kNCW * HB * 3 * 4;
     o2 = align_up(o2, 16);
     p.off_misc = static_cast<int>(o2);
-    o2 += 16 + sizeof(EpiDesc);
+    o2 += 16 + sizeof(EpiDesc) + sizeof(UnitSpan);
     o2 = align_up(o2, 8);
     p.off_bar = static_cast<int>(o2);
     o2 += (3 * nst + 2) * 8;
