@@ -35,7 +35,16 @@
 //            softmax_scale * log2 e); warp-shuffle max/sum; exp2 on MUFU.
 //       PV : lanes own output channels; V dequantized to fp16 like K;
 //            acc += p(fp16) * v(fp16) with the same mixed-precision FMA.
-//   At a unit boundary the 8 warp states are merged in shared memory.
+//   warp 9 (epilogue): at a unit boundary inside the CTA's range each
+//     consumer warp stores its raw (m, l, acc) in shared memory and arrives
+//     on a hand-off mbarrier, then goes on streaming; the epilogue warp merges
+//     the 8 warp states, writes the unit's output or publishes the partial,
+//     takes the ticket and merges the unit if it completes it. The CTA's last
+//     segment is finished by all consumer warps together.
+//
+// The grid is launched with programmatic dependent launch: every thread runs
+// griddepcontrol.wait before the first global-memory access, so only the
+// launch and the prologue overlap the previous kernel on the stream.
 //
 // Every mbarrier wait is bounded (kMaxPolls); on expiry the kernel records
 // kDevWaitTimeout in the workspace error word, stops issuing copies, drains
@@ -1083,7 +1092,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
 
 int heads_per_unit(int64_t group, int fmt) {
     // Eight heads per unit need more registers than the INT8/INT4 paths have
-    // (168 per thread at 9 warps per SM); those formats split a group of 8
+    // (168 per thread at 10 warps per SM); those formats split a group of 8
     // into two units of 4.
     if (group % 8 == 0 && fmt == kF16) return 8;
     if (group % 4 == 0) return 4;
