@@ -980,7 +980,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                     pv_accum<HB, 4, PVC>(pw, vd, acc);
                 };
                 if (nval == TW) {
-#pragma unroll 8
+#pragma unroll 4
                     for (int u = 0; u < TW; u += 2) pv_token(u);
                 } else {
                     for (int u = 0; u + hw < nval; u += 2) pv_token(u);
