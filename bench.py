@@ -16,7 +16,9 @@ asymmetric g128 (config 3) and the reference's symmetric INT4 format at g128;
 config 4 (batch 64, seqlen 32768, fp16 and INT4 asym) sharded over the ranks
 by (batch, kv-head) (strong scaling of a fixed job); an end-to-end number
 through the public op with pinned host buffers; the roofline of the fp16
-kernel against the measured HBM peak; and the CPU oracle timed on this host.
+kernel against the measured HBM peak; the KV quantize/pack (append side) and
+fp16 materialize kernels at the config-1 cache shape ("kv_kernels": us, GB/s
+and fraction of the HBM peak); and the CPU oracle timed on this host.
 
 Timing: K steps are captured in one CUDA graph (each step reads a different
 copy of the inputs; the copies together exceed 3x the L2 size, so every step
@@ -425,6 +427,70 @@ def e2e_decode_step(torch, L, dev, steps):
     return e0.elapsed_time(e1) / steps
 
 
+def time_kv_kernels(torch, L, dev, l2, peak_gbs, launches=50):
+    """The KV quantize / pack (append side) and fp16 materialize kernels at the
+    config-1/2/3 cache shape [8, 8, 4096, 128], each over freshly rotated
+    copies whose total exceeds 3x L2. Bytes are algorithmic (inputs read once,
+    outputs written once). `launches` calls are captured in a CUDA graph and
+    the replay is timed with CUDA events."""
+    b, s = C1["batch"], C1["seqlen"]
+    E = b * HKV * s * D            # elements of one K (or V) tensor
+    T = b * HKV * s                # tokens
+    G = b * HKV * (-(-s // GS)) * D  # K group-scale elements at g128
+    x_bytes = 2 * E
+    reps = copies_for(x_bytes, l2)
+    g = torch.Generator(device=dev).manual_seed(11)
+    xs = [torch.randn(b, HKV, s, D, generator=g, device=dev).half() for _ in range(reps)]
+    i8 = [L.quantize_per_token(x) for x in xs]
+    i4 = [L.quantize_k_per_channel_groupwise_int4_asym(x, GS) + L.quantize_v_per_token_int4_asym(x) for x in xs]
+    ops = [
+        ("quantize_per_token (INT8, one tensor)", lambda r: L.quantize_per_token(xs[r]),
+         x_bytes + E + 2 * T),
+        ("quantize_k_per_channel_groupwise_int4 (g128)", lambda r: L.quantize_k_per_channel_groupwise_int4(xs[r], GS),
+         x_bytes + E // 2 + 2 * G),
+        ("quantize_v_per_token_int4", lambda r: L.quantize_v_per_token_int4(xs[r]),
+         x_bytes + E // 2 + 2 * T),
+        ("quantize_k_per_channel_groupwise_int4_asym (g128)",
+         lambda r: L.quantize_k_per_channel_groupwise_int4_asym(xs[r], GS), x_bytes + E // 2 + 4 * G),
+        ("quantize_v_per_token_int4_asym", lambda r: L.quantize_v_per_token_int4_asym(xs[r]),
+         x_bytes + E // 2 + 4 * T),
+        ("dequantize_int8 (K and V to fp16)",
+         lambda r: L.dequantize_int8(i8[r][0], i8[r][1], i8[r][0], i8[r][1]), 2 * (E + 2 * T) + 2 * x_bytes),
+        ("dequantize_int4 asym (K and V to fp16)",
+         lambda r: L.dequantize_int4(i4[r][0], i4[r][1], i4[r][3], i4[r][4], GS, -1, i4[r][2], i4[r][5]),
+         2 * (E // 2) + 4 * G + 4 * T + 2 * x_bytes),
+    ]
+    res = {}
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    for name, fn, nbytes in ops:
+        # the calls are captured in one CUDA graph (the ops' host-side checks
+        # and output allocations are not part of the device time) and replayed
+        with torch.cuda.stream(st):
+            for r in range(3):
+                fn(r % reps)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=st):
+            for i in range(launches):
+                fn(i % reps)
+        graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(st):
+            e0.record(st)
+            graph.replay()
+            e1.record(st)
+        torch.cuda.synchronize()
+        del graph
+        us = e0.elapsed_time(e1) * 1e3 / launches
+        gbs = nbytes / (us * 1e-6) / 1e9
+        res[name] = {"us": us, "GB_s": gbs, "bytes": nbytes, "frac_of_hbm_peak": gbs / peak_gbs}
+    del xs, i8, i4
+    torch.cuda.empty_cache()
+    return res
+
+
 def run_ours(args):
     import torch
     world, rank, local = dist_env()
@@ -497,6 +563,8 @@ def run_ours(args):
                     c4[name]["verified"] = "last sequence of the gathered output vs CPU oracle"
             del wl
             torch.cuda.empty_cache()
+    peak, peak_kind = measured_hbm_peak()
+    kv_kernels = time_kv_kernels(torch, L, dev, l2, peak, launches=5 if args.profile else 50)
     clocks = sampler.stop()
 
     # ---- end to end through the public op (host buffers) ----
@@ -508,7 +576,6 @@ def run_ours(args):
 
     nb1 = algo_bytes("f16", b, s)
     value = world * nb1 / (head_ms * 1e-3) / 1e12
-    peak, peak_kind = measured_hbm_peak()
     achieved = nb1 / (head_ms * 1e-3) / 1e9
     line = {
         "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": world, "steps": steps,
@@ -524,6 +591,7 @@ def run_ours(args):
         "tokens_per_s": world * b / (head_ms * 1e-3),
         "formats": formats,
         "config4_sharded": c4,
+        "kv_kernels": kv_kernels,
         "e2e": {"value": world * nb1 / (e2e_ms * 1e-3) / 1e12, "unit": "TB/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
                 "what": "llmik_cuda.decode_attention with q, k, v copied from pinned host memory "

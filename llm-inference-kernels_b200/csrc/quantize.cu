@@ -36,88 +36,170 @@ __device__ __forceinline__ void load8(const __half* src, float (&f)[8]) {
     for (int i = 0; i < 8; ++i) f[i] = __half2float(h[i]);
 }
 
-__device__ __forceinline__ uint32_t pack_nibbles8(const int (&c)[8]) {
-    uint32_t w = 0;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) w |= (static_cast<uint32_t>(c[i]) & 0xFu) << (4 * i);
-    return w;
+// rint(x / s) where x / s is the IEEE fp32 quotient (round to nearest), as
+// the oracle computes it, without a division in the common case. With
+// r = RN(1/s), y = RN(x * r) lies within 2^-22.4 |x / s| of that quotient, i.e.
+// within 2.3e-5 for the |x / s| <= 128 these kernels produce; so rint(y) is
+// the quotient's nearest integer unless y lies within 1e-4 of a half-integer,
+// and only those elements pay for the exact division. (Inf / NaN inputs also
+// take the exact path.)
+// Rounding to an integer is done by adding 1.5 * 2^23 (fp32 addition rounds
+// half to even, like rintf): for |v| < 2^22 the sum holds the integer in its
+// low mantissa bits, which code_bits() reads back without a float-to-int
+// conversion.
+constexpr float kRoundMagic = 12582912.0f;  // 1.5 * 2^23
+__device__ __forceinline__ float rint_div(float x, float s, float r) {
+    const float y = __fmul_rn(x, r);
+    const float c = __fsub_rn(__fadd_rn(y, kRoundMagic), kRoundMagic);
+    if (fabsf(__fsub_rn(y, c)) < 0.4999f) return c;
+    return rintf(__fdiv_rn(x, s));
+}
+// Two's-complement bits of an integer-valued float c with |c| < 2^22.
+__device__ __forceinline__ uint32_t code_bits(float c) {
+    return static_cast<uint32_t>(__float_as_int(__fadd_rn(c, kRoundMagic)) - 0x4B400000);
 }
 
-// One 16-lane half-warp per token row (8 channels per lane).
+__device__ __forceinline__ uint32_t pack_nibbles8(const uint32_t (&c)[8]) {
+    uint32_t w = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) w |= (c[i] & 0xFu) << (4 * i);
+    return w;
+}
+// bytes 0..3 = low bytes of a, b, c, d
+__device__ __forceinline__ uint32_t pack_bytes4(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+}
+
+// One 8-lane group per kRowsPerGroup consecutive token rows, 16 channels
+// per lane; the rows' loads are issued together.
 // MODE kTokI8: int8 codes; kTokI4Sym: packed signed nibbles; kTokI4Asym:
 // packed unsigned nibbles with a zero point.
+//
+// Per element the common path is y = x * RN(1/s) rounded through the magic
+// constant; one check per lane sends a lane whose elements include a
+// near-tie (or a non-finite value) through the exact division. The symmetric
+// formats need no clamp on the common path: |x| <= absmax and s >= absmax /
+// qmax rounded to nearest, so |x / s| <= qmax (1 + 2^-24) rounds to at most
+// qmax in magnitude.
+constexpr int kRowsPerGroup = 2;
+constexpr int kLanesPerRow = 8;
+
+__device__ __forceinline__ void load16(const __half* src, float (&f)[16]) {
+    const uint4 a = *reinterpret_cast<const uint4*>(src);
+    const uint4 b = *reinterpret_cast<const uint4*>(src + 8);
+    const __half2* ha = reinterpret_cast<const __half2*>(&a);
+    const __half2* hb = reinterpret_cast<const __half2*>(&b);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 u = __half22float2(ha[i]);
+        const float2 w = __half22float2(hb[i]);
+        f[2 * i] = u.x;
+        f[2 * i + 1] = u.y;
+        f[8 + 2 * i] = w.x;
+        f[8 + 2 * i + 1] = w.y;
+    }
+}
+
 template <int MODE>
 __global__ void __launch_bounds__(256) quant_token_kernel(const __half* __restrict__ x, uint8_t* __restrict__ codes,
                                                           __half* __restrict__ scale, __half* __restrict__ zero,
                                                           long long n_rows, long long n_tok, long long dst_pos,
                                                           long long dst_buf) {
-    const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 4;
-    if (row >= n_rows) return;  // whole 16-lane groups leave together
-    const int l = threadIdx.x & 15;
-    const unsigned mask = 0xFFFFu << (threadIdx.x & 16);
-    float f[8];
-    load8(x + row * kHeadDim + l * 8, f);
+    constexpr int R = kRowsPerGroup;
+    constexpr int NL = kLanesPerRow;
+    constexpr int CH = kHeadDim / NL;  // channels per lane
+    const long long row0 = ((static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) / NL) * R;
+    if (row0 >= n_rows) return;  // whole 8-lane groups leave together
+    const int l = threadIdx.x & (NL - 1);
+    const unsigned mask = 0xFFu << (threadIdx.x & 24);
+    float f[R][CH];
+#pragma unroll
+    for (int k = 0; k < R; ++k)
+        if (row0 + k < n_rows) load16(x + (row0 + k) * kHeadDim + l * CH, f[k]);
 
-    const long long slab = row / n_tok;
-    const long long t = row - slab * n_tok;
-    const long long drow = slab * dst_buf + dst_pos + t;
-
-    if (MODE == kTokI4Asym) {
-        float mn = f[0], mx = f[0];
+    long long slab = row0 / n_tok;
+    long long t = row0 - slab * n_tok;
 #pragma unroll
-        for (int i = 1; i < 8; ++i) {
-            mn = fminf(mn, f[i]);
-            mx = fmaxf(mx, f[i]);
+    for (int k = 0; k < R; ++k) {
+        if (row0 + k >= n_rows) break;  // the same for the whole 8-lane group
+        const long long drow = slab * dst_buf + dst_pos + t;
+        if (++t == n_tok) {
+            t = 0;
+            ++slab;
         }
+        float sc, zf = 0.f, sf;
+        if (MODE == kTokI4Asym) {
+            float mn = f[k][0], mx = f[k][0];
 #pragma unroll
-        for (int m = 1; m < 16; m <<= 1) {
-            mn = fminf(mn, __shfl_xor_sync(mask, mn, m));
-            mx = fmaxf(mx, __shfl_xor_sync(mask, mx, m));
-        }
-        const float s = fmaxf(__fdiv_rn(__fsub_rn(mx, mn), 15.0f), kAsymScaleFloor);
-        const __half sh = __float2half_rn(s);
-        const __half zh = __float2half_rn(mn);
-        const float sf = __half2float(sh);
-        const float zf = __half2float(zh);
-        int c[8];
+            for (int i = 1; i < CH; ++i) {
+                mn = fminf(mn, f[k][i]);
+                mx = fmaxf(mx, f[k][i]);
+            }
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float qv = rintf(__fdiv_rn(__fsub_rn(f[i], zf), sf));
-            c[i] = static_cast<int>(fminf(fmaxf(qv, 0.0f), 15.0f));
+            for (int m = 1; m < NL; m <<= 1) {
+                mn = fminf(mn, __shfl_xor_sync(mask, mn, m));
+                mx = fmaxf(mx, __shfl_xor_sync(mask, mx, m));
+            }
+            sc = fmaxf(__fdiv_rn(__fsub_rn(mx, mn), 15.0f), kAsymScaleFloor);
+            const __half sh = __float2half_rn(sc);
+            const __half zh = __float2half_rn(mn);
+            sf = __half2float(sh);
+            zf = __half2float(zh);
+            if (l == 0) {
+                scale[drow] = sh;
+                zero[drow] = zh;
+            }
+        } else {
+            constexpr float qmax = (MODE == kTokI8) ? 127.0f : 7.0f;
+            float amax = 0.0f;
+#pragma unroll
+            for (int i = 0; i < CH; ++i) amax = fmaxf(amax, fabsf(f[k][i]));
+#pragma unroll
+            for (int m = 1; m < NL; m <<= 1) amax = fmaxf(amax, __shfl_xor_sync(mask, amax, m));
+            sc = fmaxf(__fdiv_rn(amax, qmax), 1e-8f);
+            sf = sc;
+            if (l == 0) scale[drow] = __float2half_rn(sc);
         }
-        reinterpret_cast<uint32_t*>(codes + drow * (kHeadDim / 2))[l] = pack_nibbles8(c);
-        if (l == 0) {
-            scale[drow] = sh;
-            zero[drow] = zh;
+        const float rf = __frcp_rn(sf);
+        // common path: t_i = rint(x_i / s) + 1.5 * 2^23, the code in its low bits
+        float tv[CH];
+        bool exact = false;  // some element is a near-tie, or not finite
+#pragma unroll
+        for (int i = 0; i < CH; ++i) {
+            const float xi = MODE == kTokI4Asym ? __fsub_rn(f[k][i], zf) : f[k][i];
+            const float y = __fmul_rn(xi, rf);
+            float tt = __fadd_rn(y, kRoundMagic);
+            exact |= !(fabsf(__fsub_rn(y, __fsub_rn(tt, kRoundMagic))) < 0.4999f);
+            if (MODE == kTokI4Asym) tt = fminf(fmaxf(tt, kRoundMagic), kRoundMagic + 15.0f);
+            tv[i] = tt;
         }
-        return;
+        if (exact) {  // exact quotients for the lane's elements
+            constexpr float lo = MODE == kTokI4Asym ? 0.0f : (MODE == kTokI8 ? -127.0f : -7.0f);
+            constexpr float hi = MODE == kTokI4Asym ? 15.0f : (MODE == kTokI8 ? 127.0f : 7.0f);
+#pragma unroll
+            for (int i = 0; i < CH; ++i) {
+                const float xi = MODE == kTokI4Asym ? __fsub_rn(f[k][i], zf) : f[k][i];
+                const float qv = fminf(fmaxf(rintf(__fdiv_rn(xi, sf)), lo), hi);
+                tv[i] = __fadd_rn(qv, kRoundMagic);
+            }
+        }
+        uint32_t c[CH];
+#pragma unroll
+        for (int i = 0; i < CH; ++i) c[i] = static_cast<uint32_t>(__float_as_int(tv[i]));
+        if (MODE == kTokI8) {
+            reinterpret_cast<uint4*>(codes + drow * kHeadDim)[l] =
+                make_uint4(pack_bytes4(c[0], c[1], c[2], c[3]), pack_bytes4(c[4], c[5], c[6], c[7]),
+                           pack_bytes4(c[8], c[9], c[10], c[11]), pack_bytes4(c[12], c[13], c[14], c[15]));
+        } else {
+            uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                w0 |= (c[i] & 0xFu) << (4 * i);
+                w1 |= (c[8 + i] & 0xFu) << (4 * i);
+            }
+            reinterpret_cast<uint2*>(codes + drow * (kHeadDim / 2))[l] = make_uint2(w0, w1);
+        }
     }
-
-    constexpr float qmax = (MODE == kTokI8) ? 127.0f : 7.0f;
-    float amax = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(f[i]));
-#pragma unroll
-    for (int m = 1; m < 16; m <<= 1) amax = fmaxf(amax, __shfl_xor_sync(mask, amax, m));
-    const float s = fmaxf(__fdiv_rn(amax, qmax), 1e-8f);
-    int c[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const float qv = rintf(__fdiv_rn(f[i], s));
-        c[i] = static_cast<int>(fminf(fmaxf(qv, -qmax), qmax));
-    }
-    if (MODE == kTokI8) {
-        uint32_t lo = 0, hi = 0;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            lo |= (static_cast<uint32_t>(c[i]) & 0xFFu) << (8 * i);
-            hi |= (static_cast<uint32_t>(c[4 + i]) & 0xFFu) << (8 * i);
-        }
-        reinterpret_cast<uint2*>(codes + drow * kHeadDim)[l] = make_uint2(lo, hi);
-    } else {
-        reinterpret_cast<uint32_t*>(codes + drow * (kHeadDim / 2))[l] = pack_nibbles8(c);
-    }
-    if (l == 0) scale[drow] = __float2half_rn(s);
 }
 
 // One CTA per (slab, token group): 16 channel chunks x 16 token lanes.
@@ -132,6 +214,7 @@ __global__ void __launch_bounds__(256) quant_kgroup_kernel(const __half* __restr
     __shared__ float red_b[16][kHeadDim];
     __shared__ float s_scale[kHeadDim];
     __shared__ float s_zero[kHeadDim];
+    __shared__ float s_rcp[kHeadDim];
 
     const long long blk = blockIdx.x;
     const long long slab = blk / n_groups_new;
@@ -185,34 +268,37 @@ __global__ void __launch_bounds__(256) quant_kgroup_kernel(const __half* __restr
             const __half zh = __float2half_rn(ra);
             s_scale[ch] = __half2float(sh);
             s_zero[ch] = __half2float(zh);
+            s_rcp[ch] = __frcp_rn(__half2float(sh));
             scale[gidx] = sh;
             zero[gidx] = zh;
         } else {
             const float s = fmaxf(__fdiv_rn(ra, 7.0f), 1e-8f);
             s_scale[ch] = s;
+            s_rcp[ch] = __frcp_rn(s);
             scale[gidx] = __float2half_rn(s);
         }
     }
     __syncthreads();
-    float sc[8], zc[8];
+    float sc[8], zc[8], rc[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         sc[i] = s_scale[cc * 8 + i];
         zc[i] = ASYM ? s_zero[cc * 8 + i] : 0.0f;
+        rc[i] = s_rcp[cc * 8 + i];
     }
     uint8_t* dst = codes + (slab * dst_buf + dst_pos) * (kHeadDim / 2);
     for (long long t = t0 + tl; t < t1; t += 16) {
         float f[8];
         load8(xs + t * kHeadDim + cc * 8, f);
-        int c[8];
+        uint32_t c[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             if (ASYM) {
-                const float qv = rintf(__fdiv_rn(__fsub_rn(f[i], zc[i]), sc[i]));
-                c[i] = static_cast<int>(fminf(fmaxf(qv, 0.0f), 15.0f));
+                const float qv = rint_div(__fsub_rn(f[i], zc[i]), sc[i], rc[i]);
+                c[i] = code_bits(fminf(fmaxf(qv, 0.0f), 15.0f));
             } else {
-                const float qv = rintf(__fdiv_rn(f[i], sc[i]));
-                c[i] = static_cast<int>(fminf(fmaxf(qv, -7.0f), 7.0f));
+                const float qv = rint_div(f[i], sc[i], rc[i]);
+                c[i] = code_bits(fminf(fmaxf(qv, -7.0f), 7.0f));
             }
         }
         reinterpret_cast<uint32_t*>(dst + t * (kHeadDim / 2))[cc] = pack_nibbles8(c);
@@ -226,7 +312,8 @@ lik_status launch_quant_token(int mode, const void* x, void* codes, void* scale,
                               std::string& err) {
     const long long n_rows = static_cast<long long>(n_slabs) * n_tokens;
     if (n_rows == 0) return LIK_OK;
-    const long long blocks = (n_rows + 15) / 16;
+    const long long rows_per_block = (256LL / kLanesPerRow) * kRowsPerGroup;
+    const long long blocks = (n_rows + rows_per_block - 1) / rows_per_block;
     if (blocks > 0x7fffffffLL) {
         err = "too many rows";
         return LIK_ERR_INVALID_ARGUMENT;
@@ -303,7 +390,7 @@ __global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* __restrict_
                                                      const __half* __restrict__ vs, const __half* __restrict__ vz,
                                                      __half* __restrict__ kout, __half* __restrict__ vout,
                                                      long long n_rows, long long seqlen, long long buf, int gs,
-                                                     long long ng_buf) {
+                                                     long long ng_buf, int scale_vec) {
     const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 4;
     if (row >= n_rows) return;
     const int l = threadIdx.x & 15;  // channels 8l .. 8l+7
@@ -328,6 +415,23 @@ __global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* __restrict_
         const long long g = slab * ng_buf + t / gs;
         const float sv = __half2float(vs[src]);
         const float zv = FMT == 2 ? __half2float(vz[src]) : 0.f;
+        // the lane's 8 K group scales (and zeros): one 16-byte load each when
+        // the scale tensors are 16-byte aligned, else eight 2-byte loads
+        uint4 ksv, kzv = make_uint4(0, 0, 0, 0);
+        __half* ksw = reinterpret_cast<__half*>(&ksv);
+        __half* kzw = reinterpret_cast<__half*>(&kzv);
+        if (scale_vec) {
+            ksv = reinterpret_cast<const uint4*>(ks + g * kHeadDim)[l];
+            if (FMT == 2) kzv = reinterpret_cast<const uint4*>(kz + g * kHeadDim)[l];
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                ksw[i] = ks[g * kHeadDim + 8 * l + i];
+                if (FMT == 2) kzw[i] = kz[g * kHeadDim + 8 * l + i];
+            }
+        }
+        const __half* ksh = ksw;
+        const __half* kzh = kzw;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             int ck = (a >> (4 * i)) & 0xF, cv = (b >> (4 * i)) & 0xF;
@@ -335,10 +439,9 @@ __global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* __restrict_
                 ck = ck >= 8 ? ck - 16 : ck;
                 cv = cv >= 8 ? cv - 16 : cv;
             }
-            const int ch = 8 * l + i;
-            const float sk = __half2float(ks[g * kHeadDim + ch]);
+            const float sk = __half2float(ksh[i]);
             if (FMT == 2) {
-                const float zk = __half2float(kz[g * kHeadDim + ch]);
+                const float zk = __half2float(kzh[i]);
                 k[i] = __fadd_rn(__fmul_rn(static_cast<float>(ck), sk), zk);
                 v[i] = __fadd_rn(__fmul_rn(static_cast<float>(cv), sv), zv);
             } else {
@@ -378,15 +481,17 @@ lik_status launch_dequant(int fmt, const void* kq, const void* ks, const void* k
     __half* vo = static_cast<__half*>(vout);
     const int gs = static_cast<int>(group_size > 0 ? group_size : 1);
     const unsigned nb = static_cast<unsigned>(blocks);
+    auto al16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
+    const int vec = (fmt != 0 && al16(ks) && (fmt != 2 || al16(kz))) ? 1 : 0;
     if (fmt == 0)
         dequant_kernel<0><<<nb, 256, 0, stream>>>(c(kq), h(ks), h(kz), c(vq), h(vs), h(vz), ko, vo, n_rows, seqlen,
-                                                 kv_buf_len, gs, n_groups_buf);
+                                                 kv_buf_len, gs, n_groups_buf, vec);
     else if (fmt == 1)
         dequant_kernel<1><<<nb, 256, 0, stream>>>(c(kq), h(ks), h(kz), c(vq), h(vs), h(vz), ko, vo, n_rows, seqlen,
-                                                 kv_buf_len, gs, n_groups_buf);
+                                                 kv_buf_len, gs, n_groups_buf, vec);
     else
         dequant_kernel<2><<<nb, 256, 0, stream>>>(c(kq), h(ks), h(kz), c(vq), h(vs), h(vz), ko, vo, n_rows, seqlen,
-                                                 kv_buf_len, gs, n_groups_buf);
+                                                 kv_buf_len, gs, n_groups_buf, vec);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         err = std::string("dequantize launch: ") + cudaGetErrorString(e);

@@ -170,3 +170,25 @@ def test_dequantize_ops_bit_exact(L):
                                             vq.cpu().numpy(), vs.cpu().numpy(), vz.cpu().numpy(), gs)
         np.testing.assert_array_equal(km.cpu().numpy(), rk)
         np.testing.assert_array_equal(vm.cpu().numpy(), rv)
+
+
+def test_dequantize_int4_with_unaligned_group_scales(L):
+    """K group scales / zeros that do not start on a 16-byte boundary (a view
+    one element into a larger buffer) take the per-channel load path and give
+    the same fp16 values."""
+    g = torch.Generator().manual_seed(4)
+    k = torch.randn(1, 8, 200, 128, generator=g).half().cuda()
+    v = torch.randn(1, 8, 200, 128, generator=g).half().cuda()
+    kq, ks, kz = L.quantize_k_per_channel_groupwise_int4_asym(k, 32)
+    vq, vs, vz = L.quantize_v_per_token_int4_asym(v)
+
+    def shifted(t):
+        buf = torch.empty(t.numel() + 1, dtype=t.dtype, device=t.device)
+        view = buf[1:].view(t.shape)
+        view.copy_(t)
+        assert view.data_ptr() % 16 != 0
+        return view
+
+    ref = L.dequantize_int4(kq, ks, vq, vs, 32, -1, kz, vz)
+    got = L.dequantize_int4(kq, shifted(ks), vq, vs, 32, -1, shifted(kz), vz)
+    assert torch.equal(got[0], ref[0]) and torch.equal(got[1], ref[1])

@@ -81,6 +81,54 @@ def test_asym_int4_bit_exact(L, b, s, gs):
     np.testing.assert_array_equal(z.cpu().numpy(), rz)
 
 
+def test_exact_ties_round_half_to_even(L):
+    """Rows built so that x / scale lands exactly on half-integers (scale 1):
+    the kernels' fast rounding must send these through the exact division and
+    round half to even like the oracle."""
+    halves = np.array([0.5, 1.5, 2.5, 3.5, -0.5, -1.5, -2.5, -6.5, 6.5, 5.5, -5.5, 4.5], np.float32)
+    x = np.zeros((1, 8, 16, 128), np.float32)
+    for t in range(16):
+        row = np.resize(np.roll(halves, t), 128)
+        x[0, :, t] = row
+        x[0, :, t, 0] = 127.0 if t % 2 == 0 else 7.0   # per-token absmax: scale 1 for int8 / int4
+    x16 = torch.from_numpy(x).half()
+    xc = x16.cuda()
+    q, sc = L.quantize_per_token(xc)
+    rq, rs = O.quantize_per_token(x16.numpy(), 8)
+    np.testing.assert_array_equal(q.cpu().numpy(), rq)
+    np.testing.assert_array_equal(sc.cpu().numpy(), rs.astype(np.float16))
+    q, sc = L.quantize_v_per_token_int4(xc)
+    rq, rs = O.quantize_per_token(x16.numpy(), 4)
+    np.testing.assert_array_equal(q.cpu().numpy(), O.pack_int4(rq))
+    # asymmetric: min -7.5 and max 7.5 give scale 1 and zero -7.5, so
+    # (x - zero) / scale is a half-integer wherever x is an integer
+    xa = np.resize(np.arange(-7, 8, dtype=np.float32), (1, 8, 16, 128)).copy()
+    xa[..., 0], xa[..., 1] = -7.5, 7.5
+    xa16 = torch.from_numpy(xa).half()
+    q, sc, z = L.quantize_v_per_token_int4_asym(xa16.cuda())
+    rq, rs, rz = O.quantize_v_per_token_int4_asym(xa16.numpy())
+    np.testing.assert_array_equal(q.cpu().numpy(), O.pack_int4(rq))
+    np.testing.assert_array_equal(sc.cpu().numpy(), rs)
+    np.testing.assert_array_equal(z.cpu().numpy(), rz)
+    # per-channel groups along tokens: every group holds -7.5 and 7.5 (asym:
+    # scale 1, zero -7.5) or 7 (sym: scale 1), the other tokens sit on ties
+    for gs in (16, 7):
+        t = np.arange(16)
+        col = np.resize(np.arange(-7, 8, dtype=np.float32), 16)
+        col[t % gs == 0], col[t % gs == 1] = -7.5, 7.5
+        xk = np.broadcast_to(col[None, None, :, None], (1, 8, 16, 128)).astype(np.float16)
+        q, sc, z = L.quantize_k_per_channel_groupwise_int4_asym(torch.from_numpy(xk.copy()).cuda(), gs)
+        rq, rs, rz = O.quantize_k_per_channel_groupwise_int4_asym(xk, gs)
+        np.testing.assert_array_equal(q.cpu().numpy(), O.pack_int4(rq))
+        np.testing.assert_array_equal(sc.cpu().numpy(), rs)
+        col = np.resize(halves, 16)
+        col[t % gs == 0] = 7.0
+        xk = np.broadcast_to(col[None, None, :, None], (1, 8, 16, 128)).astype(np.float16)
+        q, sc = L.quantize_k_per_channel_groupwise_int4(torch.from_numpy(xk.copy()).cuda(), gs)
+        rq, rs = O.quantize_per_channel_groupwise(xk, 4, gs)
+        np.testing.assert_array_equal(q.cpu().numpy(), O.pack_int4(rq))
+
+
 def test_constant_and_zero_rows(L):
     x = torch.zeros(1, 8, 40, 128, dtype=torch.float16)
     x[0, 1] = 3.0          # constant rows: asym range 0 -> scale floor
