@@ -29,42 +29,18 @@ namespace {
 
 constexpr float kAsymScaleFloor = 5.9604644775390625e-8f;  // 2^-24, smallest fp16 subnormal
 
-__device__ __forceinline__ void load8(const __half* src, float (&f)[8]) {
-    const uint4 u = *reinterpret_cast<const uint4*>(src);
-    const __half* h = reinterpret_cast<const __half*>(&u);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) f[i] = __half2float(h[i]);
-}
-
-// rint(x / s) where x / s is the IEEE fp32 quotient (round to nearest), as
-// the oracle computes it, without a division in the common case. With
-// r = RN(1/s), y = RN(x * r) lies within 2^-22.4 |x / s| of that quotient, i.e.
-// within 2.3e-5 for the |x / s| <= 128 these kernels produce; so rint(y) is
-// the quotient's nearest integer unless y lies within 1e-4 of a half-integer,
-// and only those elements pay for the exact division. (Inf / NaN inputs also
-// take the exact path.)
-// Rounding to an integer is done by adding 1.5 * 2^23 (fp32 addition rounds
-// half to even, like rintf): for |v| < 2^22 the sum holds the integer in its
-// low mantissa bits, which code_bits() reads back without a float-to-int
+// Codes are rint(x / s) with x / s the IEEE fp32 quotient (round to
+// nearest), as the oracle computes them, without a division in the common
+// case. With r = RN(1/s), y = RN(x * r) lies within 2^-22.4 |x / s| of that
+// quotient, i.e. within 2.3e-5 for the |x / s| <= 128 these kernels produce;
+// so y rounds to the quotient's nearest integer unless it lies within 1e-4 of
+// a half-integer, and only those elements (and non-finite ones) take the
+// exact division. Rounding adds 1.5 * 2^23 (fp32 addition rounds half to
+// even, like rintf): for |v| < 2^22 the sum holds the integer in its low
+// mantissa bits, from which the codes are packed without a float-to-int
 // conversion.
 constexpr float kRoundMagic = 12582912.0f;  // 1.5 * 2^23
-__device__ __forceinline__ float rint_div(float x, float s, float r) {
-    const float y = __fmul_rn(x, r);
-    const float c = __fsub_rn(__fadd_rn(y, kRoundMagic), kRoundMagic);
-    if (fabsf(__fsub_rn(y, c)) < 0.4999f) return c;
-    return rintf(__fdiv_rn(x, s));
-}
-// Two's-complement bits of an integer-valued float c with |c| < 2^22.
-__device__ __forceinline__ uint32_t code_bits(float c) {
-    return static_cast<uint32_t>(__float_as_int(__fadd_rn(c, kRoundMagic)) - 0x4B400000);
-}
 
-__device__ __forceinline__ uint32_t pack_nibbles8(const uint32_t (&c)[8]) {
-    uint32_t w = 0;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) w |= (c[i] & 0xFu) << (4 * i);
-    return w;
-}
 // bytes 0..3 = low bytes of a, b, c, d
 __device__ __forceinline__ uint32_t pack_bytes4(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
     return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
@@ -84,24 +60,24 @@ __device__ __forceinline__ uint32_t pack_bytes4(uint32_t a, uint32_t b, uint32_t
 constexpr int kRowsPerGroup = 2;
 constexpr int kLanesPerRow = 8;
 
-__device__ __forceinline__ void load16(const __half* src, float (&f)[16]) {
-    const uint4 a = *reinterpret_cast<const uint4*>(src);
-    const uint4 b = *reinterpret_cast<const uint4*>(src + 8);
-    const __half2* ha = reinterpret_cast<const __half2*>(&a);
-    const __half2* hb = reinterpret_cast<const __half2*>(&b);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float2 u = __half22float2(ha[i]);
-        const float2 w = __half22float2(hb[i]);
-        f[2 * i] = u.x;
-        f[2 * i + 1] = u.y;
-        f[8 + 2 * i] = w.x;
-        f[8 + 2 * i + 1] = w.y;
-    }
+// 16 halves of a row held as raw packed pairs (8 registers)
+struct Raw16 {
+    uint4 a, b;
+};
+__device__ __forceinline__ Raw16 load_raw16(const __half* src) {
+    Raw16 r;
+    r.a = *reinterpret_cast<const uint4*>(src);
+    r.b = *reinterpret_cast<const uint4*>(src + 8);
+    return r;
+}
+__device__ __forceinline__ __half2 raw_pair(const Raw16& r, int i) {  // elements 2i, 2i+1
+    const uint4& u = i < 4 ? r.a : r.b;
+    const uint32_t w = (i & 3) == 0 ? u.x : (i & 3) == 1 ? u.y : (i & 3) == 2 ? u.z : u.w;
+    return *reinterpret_cast<const __half2*>(&w);
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(256) quant_token_kernel(const __half* __restrict__ x, uint8_t* __restrict__ codes,
+__global__ void __launch_bounds__(256, 4) quant_token_kernel(const __half* __restrict__ x, uint8_t* __restrict__ codes,
                                                           __half* __restrict__ scale, __half* __restrict__ zero,
                                                           long long n_rows, long long n_tok, long long dst_pos,
                                                           long long dst_buf) {
@@ -112,10 +88,10 @@ __global__ void __launch_bounds__(256) quant_token_kernel(const __half* __restri
     if (row0 >= n_rows) return;  // whole 8-lane groups leave together
     const int l = threadIdx.x & (NL - 1);
     const unsigned mask = 0xFFu << (threadIdx.x & 24);
-    float f[R][CH];
+    Raw16 raw[R];
 #pragma unroll
     for (int k = 0; k < R; ++k)
-        if (row0 + k < n_rows) load16(x + (row0 + k) * kHeadDim + l * CH, f[k]);
+        if (row0 + k < n_rows) raw[k] = load_raw16(x + (row0 + k) * kHeadDim + l * CH);
 
     long long slab = row0 / n_tok;
     long long t = row0 - slab * n_tok;
@@ -127,14 +103,17 @@ __global__ void __launch_bounds__(256) quant_token_kernel(const __half* __restri
             t = 0;
             ++slab;
         }
+        // row statistics on packed fp16 (min / max / |x| are exact in fp16)
         float sc, zf = 0.f, sf;
         if (MODE == kTokI4Asym) {
-            float mn = f[k][0], mx = f[k][0];
+            __half2 mn2 = raw_pair(raw[k], 0), mx2 = mn2;
 #pragma unroll
-            for (int i = 1; i < CH; ++i) {
-                mn = fminf(mn, f[k][i]);
-                mx = fmaxf(mx, f[k][i]);
+            for (int i = 1; i < CH / 2; ++i) {
+                mn2 = __hmin2(mn2, raw_pair(raw[k], i));
+                mx2 = __hmax2(mx2, raw_pair(raw[k], i));
             }
+            float mn = fminf(__low2float(mn2), __high2float(mn2));
+            float mx = fmaxf(__low2float(mx2), __high2float(mx2));
 #pragma unroll
             for (int m = 1; m < NL; m <<= 1) {
                 mn = fminf(mn, __shfl_xor_sync(mask, mn, m));
@@ -151,9 +130,10 @@ __global__ void __launch_bounds__(256) quant_token_kernel(const __half* __restri
             }
         } else {
             constexpr float qmax = (MODE == kTokI8) ? 127.0f : 7.0f;
-            float amax = 0.0f;
+            __half2 am2 = __habs2(raw_pair(raw[k], 0));
 #pragma unroll
-            for (int i = 0; i < CH; ++i) amax = fmaxf(amax, fabsf(f[k][i]));
+            for (int i = 1; i < CH / 2; ++i) am2 = __hmax2(am2, __habs2(raw_pair(raw[k], i)));
+            float amax = fmaxf(__low2float(am2), __high2float(am2));
 #pragma unroll
             for (int m = 1; m < NL; m <<= 1) amax = fmaxf(amax, __shfl_xor_sync(mask, amax, m));
             sc = fmaxf(__fdiv_rn(amax, qmax), 1e-8f);
@@ -161,13 +141,19 @@ __global__ void __launch_bounds__(256) quant_token_kernel(const __half* __restri
             if (l == 0) scale[drow] = __float2half_rn(sc);
         }
         const float rf = __frcp_rn(sf);
-        // common path: t_i = rint(x_i / s) + 1.5 * 2^23, the code in its low bits
+        // common path: tv_i = rint(x_i / s) + 1.5 * 2^23, the code in its low bits
+        float xv[CH];
+#pragma unroll
+        for (int i = 0; i < CH / 2; ++i) {
+            const float2 u = __half22float2(raw_pair(raw[k], i));
+            xv[2 * i] = MODE == kTokI4Asym ? __fsub_rn(u.x, zf) : u.x;
+            xv[2 * i + 1] = MODE == kTokI4Asym ? __fsub_rn(u.y, zf) : u.y;
+        }
         float tv[CH];
         bool exact = false;  // some element is a near-tie, or not finite
 #pragma unroll
         for (int i = 0; i < CH; ++i) {
-            const float xi = MODE == kTokI4Asym ? __fsub_rn(f[k][i], zf) : f[k][i];
-            const float y = __fmul_rn(xi, rf);
+            const float y = __fmul_rn(xv[i], rf);
             float tt = __fadd_rn(y, kRoundMagic);
             exact |= !(fabsf(__fsub_rn(y, __fsub_rn(tt, kRoundMagic))) < 0.4999f);
             if (MODE == kTokI4Asym) tt = fminf(fmaxf(tt, kRoundMagic), kRoundMagic + 15.0f);
@@ -178,8 +164,7 @@ __global__ void __launch_bounds__(256) quant_token_kernel(const __half* __restri
             constexpr float hi = MODE == kTokI4Asym ? 15.0f : (MODE == kTokI8 ? 127.0f : 7.0f);
 #pragma unroll
             for (int i = 0; i < CH; ++i) {
-                const float xi = MODE == kTokI4Asym ? __fsub_rn(f[k][i], zf) : f[k][i];
-                const float qv = fminf(fmaxf(rintf(__fdiv_rn(xi, sf)), lo), hi);
+                const float qv = fminf(fmaxf(rintf(__fdiv_rn(xv[i], sf)), lo), hi);
                 tv[i] = __fadd_rn(qv, kRoundMagic);
             }
         }
@@ -202,14 +187,53 @@ __global__ void __launch_bounds__(256) quant_token_kernel(const __half* __restri
     }
 }
 
+// Eight K channels of one token to packed nibbles, with the channels'
+// scale, zero and reciprocal scale (the token kernels' rounding scheme).
+template <bool ASYM>
+__device__ __forceinline__ uint32_t quant8_k(const uint4& raw, const float (&sc)[8], const float (&zc)[8],
+                                             const float (&rc)[8]) {
+    const __half2* h = reinterpret_cast<const __half2*>(&raw);
+    float xv[8], tv[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 u = __half22float2(h[i]);
+        xv[2 * i] = ASYM ? __fsub_rn(u.x, zc[2 * i]) : u.x;
+        xv[2 * i + 1] = ASYM ? __fsub_rn(u.y, zc[2 * i + 1]) : u.y;
+    }
+    bool exact = false;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float y = __fmul_rn(xv[i], rc[i]);
+        float tt = __fadd_rn(y, kRoundMagic);
+        exact |= !(fabsf(__fsub_rn(y, __fsub_rn(tt, kRoundMagic))) < 0.4999f);
+        // asymmetric codes need the clamp (the zero point is rounded to fp16);
+        // symmetric ones cannot leave [-7, 7]: |x| <= absmax <= 7 s (1 + 2^-24)
+        if (ASYM) tt = fminf(fmaxf(tt, kRoundMagic), kRoundMagic + 15.0f);
+        tv[i] = tt;
+    }
+    if (exact) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float qv = fminf(fmaxf(rintf(__fdiv_rn(xv[i], sc[i])), ASYM ? 0.0f : -7.0f), ASYM ? 15.0f : 7.0f);
+            tv[i] = __fadd_rn(qv, kRoundMagic);
+        }
+    }
+    uint32_t w = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) w |= (static_cast<uint32_t>(__float_as_int(tv[i])) & 0xFu) << (4 * i);
+    return w;
+}
+
 // One CTA per (slab, token group): 16 channel chunks x 16 token lanes.
-// Pass 1 reduces each channel over the group's tokens; pass 2 re-reads the
-// group (L1/L2 resident) and writes packed codes.
+// Pass 1 reduces each channel over the group's tokens (on packed fp16: min,
+// max and |x| are exact); pass 2 writes packed codes. Groups of up to 128
+// tokens stay in registers between the passes; longer groups are re-read.
 template <bool ASYM>
 __global__ void __launch_bounds__(256) quant_kgroup_kernel(const __half* __restrict__ x, uint8_t* __restrict__ codes,
                                                            __half* __restrict__ scale, __half* __restrict__ zero,
                                                            long long n_groups_new, long long n_tok, int gs,
                                                            long long dst_pos, long long dst_buf, long long ng_buf) {
+    constexpr int MAXR = 8;  // token rows a thread keeps in registers
     __shared__ float red_a[16][kHeadDim];
     __shared__ float red_b[16][kHeadDim];
     __shared__ float s_scale[kHeadDim];
@@ -223,31 +247,49 @@ __global__ void __launch_bounds__(256) quant_kgroup_kernel(const __half* __restr
     const int tl = threadIdx.x >> 4;
     const long long t0 = g * gs;
     const long long t1 = min(t0 + gs, n_tok);
-    const __half* xs = x + slab * n_tok * kHeadDim;
+    const __half* xs = x + slab * n_tok * kHeadDim + cc * 8;
+    const bool in_regs = (t1 - t0) <= 16 * MAXR;  // the same for the whole CTA
 
-    float a[8], b[8];
+    const uint32_t pinf = 0x7C007C00u, ninf = 0xFC00FC00u;
+    __half2 a2[4], b2[4];  // per channel pair: min (asym) or absmax (sym); max (asym)
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        a[i] = ASYM ? INFINITY : 0.0f;  // min (asym) or absmax (sym)
-        b[i] = -INFINITY;               // max (asym)
+    for (int i = 0; i < 4; ++i) {
+        a2[i] = ASYM ? *reinterpret_cast<const __half2*>(&pinf) : __float2half2_rn(0.0f);
+        b2[i] = *reinterpret_cast<const __half2*>(&ninf);
     }
-    for (long long t = t0 + tl; t < t1; t += 16) {
-        float f[8];
-        load8(xs + t * kHeadDim + cc * 8, f);
+    auto stats = [&](const uint4& raw) {
+        const __half2* h = reinterpret_cast<const __half2*>(&raw);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < 4; ++i) {
             if (ASYM) {
-                a[i] = fminf(a[i], f[i]);
-                b[i] = fmaxf(b[i], f[i]);
+                a2[i] = __hmin2(a2[i], h[i]);
+                b2[i] = __hmax2(b2[i], h[i]);
             } else {
-                a[i] = fmaxf(a[i], fabsf(f[i]));
+                a2[i] = __hmax2(a2[i], __habs2(h[i]));
             }
         }
+    };
+    uint4 raw[MAXR];
+    if (in_regs) {
+#pragma unroll
+        for (int r = 0; r < MAXR; ++r) {
+            const long long t = t0 + tl + 16 * r;
+            if (t < t1) raw[r] = *reinterpret_cast<const uint4*>(xs + t * kHeadDim);
+        }
+#pragma unroll
+        for (int r = 0; r < MAXR; ++r)
+            if (t0 + tl + 16 * r < t1) stats(raw[r]);
+    } else {
+        for (long long t = t0 + tl; t < t1; t += 16) stats(*reinterpret_cast<const uint4*>(xs + t * kHeadDim));
     }
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        red_a[tl][cc * 8 + i] = a[i];
-        if (ASYM) red_b[tl][cc * 8 + i] = b[i];
+    for (int i = 0; i < 4; ++i) {
+        red_a[tl][cc * 8 + 2 * i] = __low2float(a2[i]);
+        red_a[tl][cc * 8 + 2 * i + 1] = __high2float(a2[i]);
+        if (ASYM) {
+            red_b[tl][cc * 8 + 2 * i] = __low2float(b2[i]);
+            red_b[tl][cc * 8 + 2 * i + 1] = __high2float(b2[i]);
+        }
     }
     __syncthreads();
     if (threadIdx.x < kHeadDim) {
@@ -287,21 +329,16 @@ __global__ void __launch_bounds__(256) quant_kgroup_kernel(const __half* __restr
         rc[i] = s_rcp[cc * 8 + i];
     }
     uint8_t* dst = codes + (slab * dst_buf + dst_pos) * (kHeadDim / 2);
-    for (long long t = t0 + tl; t < t1; t += 16) {
-        float f[8];
-        load8(xs + t * kHeadDim + cc * 8, f);
-        uint32_t c[8];
+    if (in_regs) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            if (ASYM) {
-                const float qv = rint_div(__fsub_rn(f[i], zc[i]), sc[i], rc[i]);
-                c[i] = code_bits(fminf(fmaxf(qv, 0.0f), 15.0f));
-            } else {
-                const float qv = rint_div(f[i], sc[i], rc[i]);
-                c[i] = code_bits(fminf(fmaxf(qv, -7.0f), 7.0f));
-            }
+        for (int r = 0; r < MAXR; ++r) {
+            const long long t = t0 + tl + 16 * r;
+            if (t < t1) reinterpret_cast<uint32_t*>(dst + t * (kHeadDim / 2))[cc] = quant8_k<ASYM>(raw[r], sc, zc, rc);
         }
-        reinterpret_cast<uint32_t*>(dst + t * (kHeadDim / 2))[cc] = pack_nibbles8(c);
+    } else {
+        for (long long t = t0 + tl; t < t1; t += 16)
+            reinterpret_cast<uint32_t*>(dst + t * (kHeadDim / 2))[cc] =
+                quant8_k<ASYM>(*reinterpret_cast<const uint4*>(xs + t * kHeadDim), sc, zc, rc);
     }
 }
 
