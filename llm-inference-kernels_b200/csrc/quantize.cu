@@ -420,22 +420,40 @@ lik_status launch_quant_kgroup(bool asym, const void* x, void* codes, void* scal
 namespace lik {
 namespace {
 
+// Packed fp32 pair arithmetic (sm_100: one instruction for two IEEE
+// round-to-nearest results, the same values as two scalar operations).
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 a, b, d;\n\t"
+        "mov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\t"
+        "mul.rn.f32x2 d, a, b;\n\tmov.b64 {%0, %1}, d;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 a, b, d;\n\t"
+        "mov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\t"
+        "add.rn.f32x2 d, a, b;\n\tmov.b64 {%0, %1}, d;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+
 // FMT: 0 = INT8 per token, 1 = INT4 KIVI symmetric, 2 = INT4 KIVI asymmetric.
 template <int FMT>
-__global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* __restrict__ kq, const __half* __restrict__ ks,
-                                                     const __half* __restrict__ kz, const uint8_t* __restrict__ vq,
-                                                     const __half* __restrict__ vs, const __half* __restrict__ vz,
-                                                     __half* __restrict__ kout, __half* __restrict__ vout,
-                                                     long long n_rows, long long seqlen, long long buf, int gs,
-                                                     long long ng_buf, int scale_vec) {
-    const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 4;
-    if (row >= n_rows) return;
-    const int l = threadIdx.x & 15;  // channels 8l .. 8l+7
+__device__ __forceinline__ void dequant_row(const uint8_t* __restrict__ kq, const __half* __restrict__ ks,
+                                            const __half* __restrict__ kz, const uint8_t* __restrict__ vq,
+                                            const __half* __restrict__ vs, const __half* __restrict__ vz,
+                                            __half* __restrict__ kout, __half* __restrict__ vout, long long row,
+                                            long long seqlen, long long buf, int gs, long long ng_buf, int scale_vec,
+                                            int l) {
     const long long slab = row / seqlen;
     const long long t = row - slab * seqlen;
     const long long src = slab * buf + t;
-    float k[8], v[8];
     if (FMT == 0) {
+        float k[8], v[8];
         const uint2 a = reinterpret_cast<const uint2*>(kq + src * kHeadDim)[l];
         const uint2 b = reinterpret_cast<const uint2*>(vq + src * kHeadDim)[l];
         const float sk = __half2float(ks[src]), sv = __half2float(vs[src]);
@@ -446,6 +464,16 @@ __global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* __restrict_
             v[i] = static_cast<float>(static_cast<int8_t>(b.x >> (8 * i))) * sv;
             v[4 + i] = static_cast<float>(static_cast<int8_t>(b.y >> (8 * i))) * sv;
         }
+        uint4 ko, vo;
+        __half* kh = reinterpret_cast<__half*>(&ko);
+        __half* vh = reinterpret_cast<__half*>(&vo);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            kh[i] = __float2half_rn(k[i]);
+            vh[i] = __float2half_rn(v[i]);
+        }
+        reinterpret_cast<uint4*>(kout + row * kHeadDim)[l] = ko;
+        reinterpret_cast<uint4*>(vout + row * kHeadDim)[l] = vo;
     } else {
         const uint32_t a = reinterpret_cast<const uint32_t*>(kq + src * (kHeadDim / 2))[l];
         const uint32_t b = reinterpret_cast<const uint32_t*>(vq + src * (kHeadDim / 2))[l];
@@ -467,36 +495,60 @@ __global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* __restrict_
                 if (FMT == 2) kzw[i] = kz[g * kHeadDim + 8 * l + i];
             }
         }
-        const __half* ksh = ksw;
-        const __half* kzh = kzw;
+        // nibbles -> exact floats: OR each into the mantissa of 1.5 * 2^23
+        // and subtract (signed nibbles offset by 8 first); then, per channel
+        // pair, fp32 code * scale (+ zero) with the oracle's roundings and one
+        // rounding to fp16
+        constexpr uint32_t kFlip = FMT == 1 ? 0x88888888u : 0u;
+        constexpr float kBase = FMT == 1 ? 12582920.0f : 12582912.0f;  // 1.5 * 2^23 (+ 8)
+        const uint32_t af = a ^ kFlip, bf = b ^ kFlip;
+        const __half2* ks2 = reinterpret_cast<const __half2*>(&ksv);
+        const __half2* kz2 = reinterpret_cast<const __half2*>(&kzv);
+        const float2 base = make_float2(kBase, kBase);
+        const float2 sv2 = make_float2(sv, sv), zv2 = make_float2(zv, zv);
+        uint4 ko, vo;
+        uint32_t* kw = reinterpret_cast<uint32_t*>(&ko);
+        uint32_t* vw = reinterpret_cast<uint32_t*>(&vo);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            int ck = (a >> (4 * i)) & 0xF, cv = (b >> (4 * i)) & 0xF;
-            if (FMT == 1) {
-                ck = ck >= 8 ? ck - 16 : ck;
-                cv = cv >= 8 ? cv - 16 : cv;
-            }
-            const float sk = __half2float(ksh[i]);
+        for (int i = 0; i < 4; ++i) {
+            const float2 ck = add2_rn(make_float2(__uint_as_float(0x4B400000u | ((af >> (8 * i)) & 0xFu)),
+                                                  __uint_as_float(0x4B400000u | ((af >> (8 * i + 4)) & 0xFu))),
+                                      make_float2(-base.x, -base.y));
+            const float2 cv = add2_rn(make_float2(__uint_as_float(0x4B400000u | ((bf >> (8 * i)) & 0xFu)),
+                                                  __uint_as_float(0x4B400000u | ((bf >> (8 * i + 4)) & 0xFu))),
+                                      make_float2(-base.x, -base.y));
+            float2 kf = mul2_rn(ck, __half22float2(ks2[i]));
+            float2 vf = mul2_rn(cv, sv2);
             if (FMT == 2) {
-                const float zk = __half2float(kzh[i]);
-                k[i] = __fadd_rn(__fmul_rn(static_cast<float>(ck), sk), zk);
-                v[i] = __fadd_rn(__fmul_rn(static_cast<float>(cv), sv), zv);
-            } else {
-                k[i] = static_cast<float>(ck) * sk;
-                v[i] = static_cast<float>(cv) * sv;
+                kf = add2_rn(kf, __half22float2(kz2[i]));
+                vf = add2_rn(vf, zv2);
             }
+            const __half2 kh2 = __floats2half2_rn(kf.x, kf.y);
+            const __half2 vh2 = __floats2half2_rn(vf.x, vf.y);
+            kw[i] = *reinterpret_cast<const uint32_t*>(&kh2);
+            vw[i] = *reinterpret_cast<const uint32_t*>(&vh2);
         }
+        reinterpret_cast<uint4*>(kout + row * kHeadDim)[l] = ko;
+        reinterpret_cast<uint4*>(vout + row * kHeadDim)[l] = vo;
     }
-    uint4 ko, vo;
-    __half* kh = reinterpret_cast<__half*>(&ko);
-    __half* vh = reinterpret_cast<__half*>(&vo);
+}
+
+// One 16-lane half-warp per two consecutive token rows (8 channels per lane
+// and row), so that each lane has both rows' loads in flight.
+constexpr int kDequantRows = 2;
+template <int FMT>
+__global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* __restrict__ kq, const __half* __restrict__ ks,
+                                                     const __half* __restrict__ kz, const uint8_t* __restrict__ vq,
+                                                     const __half* __restrict__ vs, const __half* __restrict__ vz,
+                                                     __half* __restrict__ kout, __half* __restrict__ vout,
+                                                     long long n_rows, long long seqlen, long long buf, int gs,
+                                                     long long ng_buf, int scale_vec) {
+    const long long row0 = ((static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 4) * kDequantRows;
+    const int l = threadIdx.x & 15;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        kh[i] = __float2half_rn(k[i]);
-        vh[i] = __float2half_rn(v[i]);
-    }
-    reinterpret_cast<uint4*>(kout + row * kHeadDim)[l] = ko;
-    reinterpret_cast<uint4*>(vout + row * kHeadDim)[l] = vo;
+    for (int k = 0; k < kDequantRows; ++k)
+        if (row0 + k < n_rows)
+            dequant_row<FMT>(kq, ks, kz, vq, vs, vz, kout, vout, row0 + k, seqlen, buf, gs, ng_buf, scale_vec, l);
 }
 
 }  // namespace
@@ -507,7 +559,7 @@ lik_status launch_dequant(int fmt, const void* kq, const void* ks, const void* k
                           std::string& err) {
     const long long n_rows = static_cast<long long>(n_slabs) * seqlen;
     if (n_rows == 0) return LIK_OK;
-    const long long blocks = (n_rows + 15) / 16;
+    const long long blocks = (n_rows + 16 * kDequantRows - 1) / (16 * kDequantRows);
     if (blocks > 0x7fffffffLL) {
         err = "too many rows";
         return LIK_ERR_INVALID_ARGUMENT;
