@@ -228,8 +228,9 @@ __device__ __forceinline__ uint32_t quant8_k(const uint4& raw, const float (&sc)
 // Pass 1 reduces each channel over the group's tokens (on packed fp16: min,
 // max and |x| are exact); pass 2 writes packed codes. Groups of up to 128
 // tokens stay in registers between the passes; longer groups are re-read.
+// (register caps measured best on B200: 3 CTAs per SM with zero points, 4 without)
 template <bool ASYM>
-__global__ void __launch_bounds__(256) quant_kgroup_kernel(const __half* __restrict__ x, uint8_t* __restrict__ codes,
+__global__ void __launch_bounds__(256, ASYM ? 3 : 4) quant_kgroup_kernel(const __half* __restrict__ x, uint8_t* __restrict__ codes,
                                                            __half* __restrict__ scale, __half* __restrict__ zero,
                                                            long long n_groups_new, long long n_tok, int gs,
                                                            long long dst_pos, long long dst_buf, long long ng_buf) {
