@@ -171,6 +171,27 @@ lik_status lik_decode_attention_paged(
     int64_t group_size, float softmax_scale,
     void* workspace, size_t workspace_bytes, void* stream);
 
+/* Append new tokens into a paged cache (the layout lik_decode_attention_paged
+ * reads; no reference counterpart: the reference appends only to contiguous
+ * caches, with torch.cat). x: the new K or the new V, [n_tokens, n_kv_heads,
+ * 128] fp16, contiguous. slot_mapping: [n_tokens] int64; token i is written
+ * to row slot % block_size of block slot / block_size; slots < 0 (padding) or
+ * >= num_blocks * block_size are skipped. row_format: 0 fp16 (cache rows of
+ * 128 halves, scale/zero unused), 1 INT8 per token (codes + scale), 2 INT4
+ * per token symmetric (KIVI V: packed signed nibbles + scale), 3 INT4 per
+ * token asymmetric (V of the asymmetric format: unsigned nibbles + scale +
+ * zero). cache [num_blocks, n_kv_heads, block_size, 128 | 64]; scale, zero
+ * [num_blocks, n_kv_heads, block_size] fp16. Codes and scales are those of the
+ * contiguous quantizers (bit-exact with the oracle). The INT4 K format is
+ * quantized per channel over groups of tokens and cannot be appended one
+ * token at a time: use lik_quantize_k_per_channel_groupwise_int4[_asym] on a
+ * block's rows once its group is complete. */
+lik_status lik_paged_append(
+    int row_format, const void* x, const int64_t* slot_mapping,
+    int64_t n_tokens, int64_t n_kv_heads, int64_t head_dim,
+    void* cache, void* scale, void* zero,
+    int64_t num_blocks, int64_t block_size, void* stream);
+
 /* ---- KV quantize / pack --------------------------------------------- */
 /*
  * Source x: [batch, n_kv_heads, n_tokens, head_dim] fp16, contiguous.

@@ -307,6 +307,25 @@ lik_status lik_quantize_k_per_channel_groupwise_int4_asym(const void* x, int8_t*
                         dst_buf_len, n_groups_buf, stream);
 }
 
+lik_status lik_paged_append(int row_format, const void* x, const int64_t* slot_mapping, int64_t n_tokens,
+                            int64_t n_kv_heads, int64_t head_dim, void* cache, void* scale, void* zero,
+                            int64_t num_blocks, int64_t block_size, void* stream) {
+    if (row_format < 0 || row_format > 3) return fail(LIK_ERR_INVALID_ARGUMENT, "unknown row_format");
+    if (n_tokens < 0 || n_kv_heads <= 0 || num_blocks < 0 || block_size <= 0 || block_size > (1 << 20))
+        return fail(LIK_ERR_INVALID_ARGUMENT, "need n_tokens >= 0, n_kv_heads > 0, num_blocks >= 0, block_size > 0");
+    if (head_dim != kHeadDim) return fail(LIK_ERR_UNSUPPORTED, "only head_dim=128 supported");
+    if (n_tokens == 0) return LIK_OK;
+    if (!x || !slot_mapping || !cache) return fail(LIK_ERR_INVALID_ARGUMENT, "null tensor pointer");
+    if (row_format != 0 && !scale) return fail(LIK_ERR_INVALID_ARGUMENT, "null scale pointer");
+    if (row_format == 3 && !zero) return fail(LIK_ERR_INVALID_ARGUMENT, "null zero-point pointer");
+    if (!aligned16(x) || !aligned16(cache)) return fail(LIK_ERR_MISALIGNED, "x and cache must be 16-byte aligned");
+    if (n_tokens > (int64_t{1} << 40) / n_kv_heads) return fail(LIK_ERR_INVALID_ARGUMENT, "too many tokens");
+    std::string err;
+    const lik_status s = launch_paged_append(row_format, x, slot_mapping, n_tokens, n_kv_heads, cache, scale, zero,
+                                             num_blocks, block_size, as_stream(stream), err);
+    return s == LIK_OK ? s : fail(s, err);
+}
+
 static lik_status dequant_common(int fmt, const void* kq, const void* ks, const void* kz, const void* vq,
                                  const void* vs, const void* vz, void* ko, void* vo, int64_t batch, int64_t n_kv_heads,
                                  int64_t seqlen, int64_t kv_buf_len, int64_t head_dim, int64_t group_size,

@@ -64,6 +64,9 @@ lik_status launch_quant_kgroup(bool asym, const void* x, void* codes, void* scal
                                int64_t dst_pos, int64_t dst_buf_len, int64_t n_groups_buf,
                                cudaStream_t stream, std::string& err);
 
+lik_status launch_paged_append(int row_format, const void* x, const int64_t* slots, int64_t n_tokens,
+                               int64_t n_heads, void* cache, void* scale, void* zero, int64_t num_blocks,
+                               int64_t block_size, cudaStream_t stream, std::string& err);
 lik_status launch_dequant(int fmt, const void* kq, const void* ks, const void* kz, const void* vq, const void* vs,
                           const void* vz, void* kout, void* vout, int64_t n_slabs, int64_t seqlen,
                           int64_t kv_buf_len, int64_t group_size, int64_t n_groups_buf, cudaStream_t stream,

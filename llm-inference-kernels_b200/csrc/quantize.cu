@@ -76,6 +76,97 @@ __device__ __forceinline__ __half2 raw_pair(const Raw16& r, int i) {  // element
     return *reinterpret_cast<const __half2*>(&w);
 }
 
+// Quantize one token row held by an 8-lane group (16 channels per lane) into
+// destination row drow: statistics, scale (and zero), codes, packed stores.
+template <int MODE>
+__device__ __forceinline__ void quant_row(const Raw16& raw, long long drow, uint8_t* __restrict__ codes,
+                                          __half* __restrict__ scale, __half* __restrict__ zero, int l,
+                                          unsigned mask) {
+    constexpr int NL = kLanesPerRow;
+    constexpr int CH = kHeadDim / NL;
+    // row statistics on packed fp16 (min / max / |x| are exact in fp16)
+    float sc, zf = 0.f, sf;
+    if (MODE == kTokI4Asym) {
+        __half2 mn2 = raw_pair(raw, 0), mx2 = mn2;
+#pragma unroll
+        for (int i = 1; i < CH / 2; ++i) {
+            mn2 = __hmin2(mn2, raw_pair(raw, i));
+            mx2 = __hmax2(mx2, raw_pair(raw, i));
+        }
+        float mn = fminf(__low2float(mn2), __high2float(mn2));
+        float mx = fmaxf(__low2float(mx2), __high2float(mx2));
+#pragma unroll
+        for (int m = 1; m < NL; m <<= 1) {
+            mn = fminf(mn, __shfl_xor_sync(mask, mn, m));
+            mx = fmaxf(mx, __shfl_xor_sync(mask, mx, m));
+        }
+        sc = fmaxf(__fdiv_rn(__fsub_rn(mx, mn), 15.0f), kAsymScaleFloor);
+        const __half sh = __float2half_rn(sc);
+        const __half zh = __float2half_rn(mn);
+        sf = __half2float(sh);
+        zf = __half2float(zh);
+        if (l == 0) {
+            scale[drow] = sh;
+            zero[drow] = zh;
+        }
+    } else {
+        constexpr float qmax = (MODE == kTokI8) ? 127.0f : 7.0f;
+        __half2 am2 = __habs2(raw_pair(raw, 0));
+#pragma unroll
+        for (int i = 1; i < CH / 2; ++i) am2 = __hmax2(am2, __habs2(raw_pair(raw, i)));
+        float amax = fmaxf(__low2float(am2), __high2float(am2));
+#pragma unroll
+        for (int m = 1; m < NL; m <<= 1) amax = fmaxf(amax, __shfl_xor_sync(mask, amax, m));
+        sc = fmaxf(__fdiv_rn(amax, qmax), 1e-8f);
+        sf = sc;
+        if (l == 0) scale[drow] = __float2half_rn(sc);
+    }
+    const float rf = __frcp_rn(sf);
+    // common path: tv_i = rint(x_i / s) + 1.5 * 2^23, the code in its low bits
+    float xv[CH];
+#pragma unroll
+    for (int i = 0; i < CH / 2; ++i) {
+        const float2 u = __half22float2(raw_pair(raw, i));
+        xv[2 * i] = MODE == kTokI4Asym ? __fsub_rn(u.x, zf) : u.x;
+        xv[2 * i + 1] = MODE == kTokI4Asym ? __fsub_rn(u.y, zf) : u.y;
+    }
+    float tv[CH];
+    bool exact = false;  // some element is a near-tie, or not finite
+#pragma unroll
+    for (int i = 0; i < CH; ++i) {
+        const float y = __fmul_rn(xv[i], rf);
+        float tt = __fadd_rn(y, kRoundMagic);
+        exact |= !(fabsf(__fsub_rn(y, __fsub_rn(tt, kRoundMagic))) < 0.4999f);
+        if (MODE == kTokI4Asym) tt = fminf(fmaxf(tt, kRoundMagic), kRoundMagic + 15.0f);
+        tv[i] = tt;
+    }
+    if (exact) {  // exact quotients for the lane's elements
+        constexpr float lo = MODE == kTokI4Asym ? 0.0f : (MODE == kTokI8 ? -127.0f : -7.0f);
+        constexpr float hi = MODE == kTokI4Asym ? 15.0f : (MODE == kTokI8 ? 127.0f : 7.0f);
+#pragma unroll
+        for (int i = 0; i < CH; ++i) {
+            const float qv = fminf(fmaxf(rintf(__fdiv_rn(xv[i], sf)), lo), hi);
+            tv[i] = __fadd_rn(qv, kRoundMagic);
+        }
+    }
+    uint32_t c[CH];
+#pragma unroll
+    for (int i = 0; i < CH; ++i) c[i] = static_cast<uint32_t>(__float_as_int(tv[i]));
+    if (MODE == kTokI8) {
+        reinterpret_cast<uint4*>(codes + drow * kHeadDim)[l] =
+            make_uint4(pack_bytes4(c[0], c[1], c[2], c[3]), pack_bytes4(c[4], c[5], c[6], c[7]),
+                       pack_bytes4(c[8], c[9], c[10], c[11]), pack_bytes4(c[12], c[13], c[14], c[15]));
+    } else {
+        uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            w0 |= (c[i] & 0xFu) << (4 * i);
+            w1 |= (c[8 + i] & 0xFu) << (4 * i);
+        }
+        reinterpret_cast<uint2*>(codes + drow * (kHeadDim / 2))[l] = make_uint2(w0, w1);
+    }
+}
+
 template <int MODE>
 __global__ void __launch_bounds__(256, 4) quant_token_kernel(const __half* __restrict__ x, uint8_t* __restrict__ codes,
                                                           __half* __restrict__ scale, __half* __restrict__ zero,
@@ -103,86 +194,49 @@ __global__ void __launch_bounds__(256, 4) quant_token_kernel(const __half* __res
             t = 0;
             ++slab;
         }
-        // row statistics on packed fp16 (min / max / |x| are exact in fp16)
-        float sc, zf = 0.f, sf;
-        if (MODE == kTokI4Asym) {
-            __half2 mn2 = raw_pair(raw[k], 0), mx2 = mn2;
+        quant_row<MODE>(raw[k], drow, codes, scale, zero, l, mask);
+    }
+}
+
+// Append of new tokens into a paged cache [num_blocks, n_heads, block_size,
+// row]: source rows are (token, kv head) of x [n_tokens, n_heads, 128]; token
+// i goes to slot slots[i] = block * block_size + offset (slots < 0 or past the
+// cache are skipped). MODE kAppendF16 copies fp16 rows; the others quantize
+// per token like quant_token_kernel.
+constexpr int kAppendF16 = -1;
+template <int MODE>
+__global__ void __launch_bounds__(256, 4) paged_append_kernel(const __half* __restrict__ x,
+                                                           const long long* __restrict__ slots, long long n_rows,
+                                                           int n_heads, int block_size, long long n_slots,
+                                                           uint8_t* __restrict__ codes, __half* __restrict__ scale,
+                                                           __half* __restrict__ zero) {
+    constexpr int R = kRowsPerGroup;
+    constexpr int NL = kLanesPerRow;
+    constexpr int CH = kHeadDim / NL;
+    const long long row0 = ((static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) / NL) * R;
+    if (row0 >= n_rows) return;
+    const int l = threadIdx.x & (NL - 1);
+    const unsigned mask = 0xFFu << (threadIdx.x & 24);
+    Raw16 raw[R];
 #pragma unroll
-            for (int i = 1; i < CH / 2; ++i) {
-                mn2 = __hmin2(mn2, raw_pair(raw[k], i));
-                mx2 = __hmax2(mx2, raw_pair(raw[k], i));
-            }
-            float mn = fminf(__low2float(mn2), __high2float(mn2));
-            float mx = fmaxf(__low2float(mx2), __high2float(mx2));
+    for (int k = 0; k < R; ++k)
+        if (row0 + k < n_rows) raw[k] = load_raw16(x + (row0 + k) * kHeadDim + l * CH);
 #pragma unroll
-            for (int m = 1; m < NL; m <<= 1) {
-                mn = fminf(mn, __shfl_xor_sync(mask, mn, m));
-                mx = fmaxf(mx, __shfl_xor_sync(mask, mx, m));
-            }
-            sc = fmaxf(__fdiv_rn(__fsub_rn(mx, mn), 15.0f), kAsymScaleFloor);
-            const __half sh = __float2half_rn(sc);
-            const __half zh = __float2half_rn(mn);
-            sf = __half2float(sh);
-            zf = __half2float(zh);
-            if (l == 0) {
-                scale[drow] = sh;
-                zero[drow] = zh;
-            }
+    for (int k = 0; k < R; ++k) {
+        const long long row = row0 + k;
+        if (row >= n_rows) break;  // the same for the whole 8-lane group
+        const long long tok = row / n_heads;
+        const int h = static_cast<int>(row - tok * n_heads);
+        const long long slot = slots[tok];
+        if (slot < 0 || slot >= n_slots) continue;
+        const long long blk = slot / block_size;
+        const long long drow = (blk * n_heads + h) * block_size + (slot - blk * block_size);
+        if (MODE == kAppendF16) {
+            uint4* dst = reinterpret_cast<uint4*>(codes + drow * (kHeadDim * 2)) + 2 * l;
+            dst[0] = raw[k].a;
+            dst[1] = raw[k].b;
         } else {
-            constexpr float qmax = (MODE == kTokI8) ? 127.0f : 7.0f;
-            __half2 am2 = __habs2(raw_pair(raw[k], 0));
-#pragma unroll
-            for (int i = 1; i < CH / 2; ++i) am2 = __hmax2(am2, __habs2(raw_pair(raw[k], i)));
-            float amax = fmaxf(__low2float(am2), __high2float(am2));
-#pragma unroll
-            for (int m = 1; m < NL; m <<= 1) amax = fmaxf(amax, __shfl_xor_sync(mask, amax, m));
-            sc = fmaxf(__fdiv_rn(amax, qmax), 1e-8f);
-            sf = sc;
-            if (l == 0) scale[drow] = __float2half_rn(sc);
-        }
-        const float rf = __frcp_rn(sf);
-        // common path: tv_i = rint(x_i / s) + 1.5 * 2^23, the code in its low bits
-        float xv[CH];
-#pragma unroll
-        for (int i = 0; i < CH / 2; ++i) {
-            const float2 u = __half22float2(raw_pair(raw[k], i));
-            xv[2 * i] = MODE == kTokI4Asym ? __fsub_rn(u.x, zf) : u.x;
-            xv[2 * i + 1] = MODE == kTokI4Asym ? __fsub_rn(u.y, zf) : u.y;
-        }
-        float tv[CH];
-        bool exact = false;  // some element is a near-tie, or not finite
-#pragma unroll
-        for (int i = 0; i < CH; ++i) {
-            const float y = __fmul_rn(xv[i], rf);
-            float tt = __fadd_rn(y, kRoundMagic);
-            exact |= !(fabsf(__fsub_rn(y, __fsub_rn(tt, kRoundMagic))) < 0.4999f);
-            if (MODE == kTokI4Asym) tt = fminf(fmaxf(tt, kRoundMagic), kRoundMagic + 15.0f);
-            tv[i] = tt;
-        }
-        if (exact) {  // exact quotients for the lane's elements
-            constexpr float lo = MODE == kTokI4Asym ? 0.0f : (MODE == kTokI8 ? -127.0f : -7.0f);
-            constexpr float hi = MODE == kTokI4Asym ? 15.0f : (MODE == kTokI8 ? 127.0f : 7.0f);
-#pragma unroll
-            for (int i = 0; i < CH; ++i) {
-                const float qv = fminf(fmaxf(rintf(__fdiv_rn(xv[i], sf)), lo), hi);
-                tv[i] = __fadd_rn(qv, kRoundMagic);
-            }
-        }
-        uint32_t c[CH];
-#pragma unroll
-        for (int i = 0; i < CH; ++i) c[i] = static_cast<uint32_t>(__float_as_int(tv[i]));
-        if (MODE == kTokI8) {
-            reinterpret_cast<uint4*>(codes + drow * kHeadDim)[l] =
-                make_uint4(pack_bytes4(c[0], c[1], c[2], c[3]), pack_bytes4(c[4], c[5], c[6], c[7]),
-                           pack_bytes4(c[8], c[9], c[10], c[11]), pack_bytes4(c[12], c[13], c[14], c[15]));
-        } else {
-            uint32_t w0 = 0, w1 = 0;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                w0 |= (c[i] & 0xFu) << (4 * i);
-                w1 |= (c[8 + i] & 0xFu) << (4 * i);
-            }
-            reinterpret_cast<uint2*>(codes + drow * (kHeadDim / 2))[l] = make_uint2(w0, w1);
+            quant_row<MODE < 0 ? 0 : MODE>(raw[k], drow, codes, scale, zero, l, mask);
         }
     }
 }
@@ -377,6 +431,39 @@ lik_status launch_quant_token(int mode, const void* x, void* codes, void* scale,
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         err = std::string("quantize launch: ") + cudaGetErrorString(e);
+        return LIK_ERR_CUDA;
+    }
+    return LIK_OK;
+}
+
+lik_status launch_paged_append(int row_format, const void* x, const int64_t* slots, int64_t n_tokens,
+                               int64_t n_heads, void* cache, void* scale, void* zero, int64_t num_blocks,
+                               int64_t block_size, cudaStream_t stream, std::string& err) {
+    const long long n_rows = static_cast<long long>(n_tokens) * n_heads;
+    if (n_rows == 0) return LIK_OK;
+    const long long rows_per_block = (256LL / kLanesPerRow) * kRowsPerGroup;
+    const long long blocks = (n_rows + rows_per_block - 1) / rows_per_block;
+    if (blocks > 0x7fffffffLL) {
+        err = "too many rows";
+        return LIK_ERR_INVALID_ARGUMENT;
+    }
+    const __half* xh = static_cast<const __half*>(x);
+    const long long* sl = reinterpret_cast<const long long*>(slots);
+    uint8_t* c = static_cast<uint8_t*>(cache);
+    __half* s = static_cast<__half*>(scale);
+    __half* z = static_cast<__half*>(zero);
+    const long long n_slots = static_cast<long long>(num_blocks) * block_size;
+    const unsigned nb = static_cast<unsigned>(blocks);
+    const int nh = static_cast<int>(n_heads), bs = static_cast<int>(block_size);
+    switch (row_format) {
+        case 0: paged_append_kernel<kAppendF16><<<nb, 256, 0, stream>>>(xh, sl, n_rows, nh, bs, n_slots, c, s, z); break;
+        case 1: paged_append_kernel<kTokI8><<<nb, 256, 0, stream>>>(xh, sl, n_rows, nh, bs, n_slots, c, s, z); break;
+        case 2: paged_append_kernel<kTokI4Sym><<<nb, 256, 0, stream>>>(xh, sl, n_rows, nh, bs, n_slots, c, s, z); break;
+        default: paged_append_kernel<kTokI4Asym><<<nb, 256, 0, stream>>>(xh, sl, n_rows, nh, bs, n_slots, c, s, z); break;
+    }
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        err = std::string("paged append launch: ") + cudaGetErrorString(e);
         return LIK_ERR_CUDA;
     }
     return LIK_OK;

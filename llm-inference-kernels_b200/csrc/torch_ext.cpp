@@ -396,6 +396,56 @@ torch::Tensor paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, tor
     return out;
 }
 
+// Append new tokens x [n_tokens, n_kv_heads, 128] fp16 (the new K or V) into
+// a paged cache at slot_mapping (int64 [n_tokens]; negative = skip). The row
+// format follows the cache: fp16 cache -> copy; int8 cache with 128-byte rows
+// -> INT8 per token (scale); 64-byte rows -> INT4 per token (scale, and zero
+// for the asymmetric format).
+void paged_append(torch::Tensor x, torch::Tensor slot_mapping, torch::Tensor cache,
+                  c10::optional<torch::Tensor> scale, c10::optional<torch::Tensor> zero) {
+    check_cuda(x, "x");
+    check_cuda(slot_mapping, "slot_mapping");
+    check_cuda(cache, "cache");
+    TORCH_CHECK(x.scalar_type() == torch::kHalf && x.dim() == 3 && x.size(2) == 128,
+                "x must be fp16 [n_tokens, n_kv_heads, 128]");
+    TORCH_CHECK(slot_mapping.scalar_type() == torch::kInt64 && slot_mapping.dim() == 1 &&
+                    slot_mapping.size(0) == x.size(0),
+                "slot_mapping must be int64 [n_tokens]");
+    TORCH_CHECK(cache.dim() == 4 && cache.size(1) == x.size(1),
+                "cache must be [num_blocks, n_kv_heads, block_size, row] with x's head count");
+    int fmt;
+    if (cache.scalar_type() == torch::kHalf) {
+        TORCH_CHECK(cache.size(3) == 128, "fp16 cache rows must be 128 wide");
+        fmt = 0;
+    } else {
+        TORCH_CHECK(cache.scalar_type() == torch::kInt8, "cache must be fp16 or int8 codes");
+        TORCH_CHECK(scale.has_value(), "a quantized cache needs its per-token scale");
+        if (cache.size(3) == 128) {
+            fmt = 1;
+        } else {
+            TORCH_CHECK(cache.size(3) == 64, "packed INT4 rows must be 64 bytes");
+            fmt = zero.has_value() ? 3 : 2;
+        }
+    }
+    for (const auto* t : {&scale, &zero}) {
+        if (!t->has_value()) continue;
+        const auto& u = **t;
+        check_cuda(u, "scale / zero");
+        TORCH_CHECK(u.scalar_type() == torch::kHalf && u.dim() == 3 && u.size(0) == cache.size(0) &&
+                        u.size(1) == cache.size(1) && u.size(2) == cache.size(2),
+                    "scale / zero must be fp16 [num_blocks, n_kv_heads, block_size]");
+        check_same_device(x, u);
+    }
+    check_same_device(x, slot_mapping);
+    check_same_device(x, cache);
+    const c10::cuda::CUDAGuard guard(x.device());
+    ok_or_throw(lik_paged_append(fmt, x.data_ptr(), slot_mapping.data_ptr<int64_t>(), x.size(0), x.size(1), 128,
+                                 cache.data_ptr(), scale.has_value() ? scale->data_ptr() : nullptr,
+                                 zero.has_value() ? zero->data_ptr() : nullptr, cache.size(0), cache.size(2),
+                                 cur_stream()),
+                "paged_append");
+}
+
 // ---------------------------------------------------------------- dequantize
 
 std::tuple<torch::Tensor, torch::Tensor> dequant_out(const torch::Tensor& codes, int64_t s) {
@@ -499,6 +549,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           py::arg("softmax_scale"), py::arg("max_context_len"), py::arg("k_scale") = py::none(),
           py::arg("v_scale") = py::none(), py::arg("group_size") = 0, py::arg("k_zero") = py::none(),
           py::arg("v_zero") = py::none());
+    m.def("paged_append", &paged_append,
+          "Append new K or V tokens into a paged cache at slot_mapping (fp16 copy or per-token quantize)",
+          py::arg("x"), py::arg("slot_mapping"), py::arg("cache"), py::arg("scale") = py::none(),
+          py::arg("zero") = py::none());
     m.def("dequantize_int8", &dequantize_int8, "INT8 per-token KV -> fp16 K, V (first seqlen positions)",
           py::arg("k_q"), py::arg("k_scale"), py::arg("v_q"), py::arg("v_scale"), py::arg("seqlen") = -1);
     m.def("dequantize_int4", &dequantize_int4,

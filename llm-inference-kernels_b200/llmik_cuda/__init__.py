@@ -53,6 +53,7 @@ quantize_k_per_channel_groupwise_int4_into = _C.quantize_k_per_channel_groupwise
 dequantize_int8 = _C.dequantize_int8
 paged_decode_attention = _C.paged_decode_attention
 dequantize_int4 = _C.dequantize_int4
+paged_append = _C.paged_append
 
 LIBRARY_PATH = _os.path.join(_here, "libllmik_b200.so")
 
@@ -61,6 +62,6 @@ __all__ = [
     "quantize_k_per_channel_groupwise_int4", "quantize_v_per_token_int4", "decode_attention_int4",
     "quantize_k_per_channel_groupwise_int4_asym", "quantize_v_per_token_int4_asym",
     "decode_attention_int4_asym", "quantize_per_token_into", "quantize_v_per_token_int4_into",
-    "quantize_k_per_channel_groupwise_int4_into", "dequantize_int8", "dequantize_int4", "paged_decode_attention",
+    "quantize_k_per_channel_groupwise_int4_into", "dequantize_int8", "dequantize_int4", "paged_decode_attention", "paged_append",
     "LIBRARY_PATH",
 ]

@@ -46,6 +46,7 @@ SIGNATURES = {
                                                               _i64, _i64, _i64, _p]),
     "lik_decode_attention_paged": (_int, [_int, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64,
                                           _i64, _i64, _i64, _i64, _f, _p, _sz, _p]),
+    "lik_paged_append": (_int, [_int, _p, _p, _i64, _i64, _i64, _p, _p, _p, _i64, _i64, _p]),
     "lik_dequantize_int8": (_int, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p]),
     "lik_dequantize_int4": (_int, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p]),
     "lik_dequantize_int4_asym": (_int, [_p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64,

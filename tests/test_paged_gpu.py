@@ -99,3 +99,100 @@ def test_paged_matches_oracle(L, fmt, bs, gs):
     for b, l in enumerate(lens):
         ref = O.decode_attention(q[b:b + 1].numpy(), kd[b:b + 1], vd[b:b + 1], SCALE, seqlen=l)
         assert_attn_close(out[b:b + 1], ref)
+
+
+def _contig_rows(L, fmt, x):
+    """Reference rows for x [n_tokens, H, 128]: the contiguous quantizers run on
+    x viewed as one sequence [1, H, n_tokens, 128]; returns per-(token, head)
+    codes / scale / zero laid out [n_tokens, H, ...]."""
+    xc = x.permute(1, 0, 2).unsqueeze(0).contiguous()
+    if fmt == "f16":
+        return (x,)
+    if fmt == "int8":
+        q, s = L.quantize_per_token(xc)
+        return q[0].permute(1, 0, 2), s[0].permute(1, 0)
+    if fmt == "int4":
+        q, s = L.quantize_v_per_token_int4(xc)
+        return q[0].permute(1, 0, 2), s[0].permute(1, 0)
+    q, s, z = L.quantize_v_per_token_int4_asym(xc)
+    return q[0].permute(1, 0, 2), s[0].permute(1, 0), z[0].permute(1, 0)
+
+
+@pytest.mark.parametrize("fmt", ["f16", "int8", "int4", "int4_asym"])
+def test_paged_append_matches_contiguous_quantizers(L, fmt):
+    """Tokens appended through a scrambled slot mapping (with padding slots)
+    land in the right block rows with the contiguous quantizers' codes,
+    scales and zeros; rows no slot names stay untouched."""
+    g = torch.Generator().manual_seed(11)
+    T, H, bs, nb = 45, 8, 16, 6
+    x = torch.randn(T, H, 128, generator=g).half().cuda()
+    x[3, 2, 5] = 40.0                              # an outlier row
+    slots = torch.randperm(nb * bs, generator=g)[:T].clone()
+    slots[[4, 17, 30]] = -1                        # padding tokens
+    slots_d = slots.cuda()
+    row = 128 if fmt in ("f16", "int8") else 64
+    dt = torch.float16 if fmt == "f16" else torch.int8
+    cache = torch.full((nb, H, bs, row), 3, dtype=dt, device="cuda")
+    scale = torch.full((nb, H, bs), 9.0, dtype=torch.float16, device="cuda") if fmt != "f16" else None
+    zero = torch.full((nb, H, bs), 9.0, dtype=torch.float16, device="cuda") if fmt == "int4_asym" else None
+    before = cache.clone()
+    L.paged_append(x, slots_d, cache, scale, zero)
+    ref = _contig_rows(L, fmt, x)
+    written = torch.zeros(nb, bs, dtype=torch.bool)
+    for t in range(T):
+        s = int(slots[t])
+        if s < 0:
+            continue
+        blk, off = divmod(s, bs)
+        written[blk, off] = True
+        assert torch.equal(cache[blk, :, off], ref[0][t])
+        if scale is not None:
+            assert torch.equal(scale[blk, :, off], ref[1][t])
+        if zero is not None:
+            assert torch.equal(zero[blk, :, off], ref[2][t])
+    untouched = ~written.cuda()
+    assert torch.equal(cache.permute(0, 2, 1, 3)[untouched], before.permute(0, 2, 1, 3)[untouched])
+
+
+def test_paged_append_then_decode(L):
+    """A paged INT8 cache filled by paged_append (prefill, then one decode
+    token per sequence) attends like the oracle over the dequantized rows."""
+    g = torch.Generator().manual_seed(12)
+    B, H, HQ, bs = 3, 8, 32, 16
+    lens = [40, 1, 77]
+    n_blocks = sum(-(-(l + 1) // bs) for l in lens) + 2
+    perm = torch.randperm(n_blocks, generator=g).tolist()
+    maxb = max(-(-(l + 1) // bs) for l in lens)
+    table = torch.zeros(B, maxb, dtype=torch.int32)
+    k = 0
+    for b, l in enumerate(lens):
+        for blk in range(-(-(l + 1) // bs)):
+            table[b, blk] = perm[k]
+            k += 1
+    kc = torch.zeros(n_blocks, H, bs, 128, dtype=torch.int8, device="cuda")
+    vc = torch.zeros_like(kc)
+    ks = torch.ones(n_blocks, H, bs, dtype=torch.float16, device="cuda")
+    vs = torch.ones_like(ks)
+    seqs = [torch.randn(l + 1, H, 128, generator=g).half() for l in lens]   # prefill + 1 new token
+
+    def slots_for(b, t0, t1):
+        return torch.tensor([int(table[b, t // bs]) * bs + t % bs for t in range(t0, t1)], dtype=torch.int64)
+
+    for phase in ("prefill", "decode"):
+        for b, l in enumerate(lens):
+            t0, t1 = (0, l) if phase == "prefill" else (l, l + 1)
+            xk = seqs[b][t0:t1].cuda()
+            sl = slots_for(b, t0, t1).cuda()
+            L.paged_append(xk, sl, kc, ks)
+            L.paged_append(xk.flip(2).contiguous(), sl, vc, vs)   # V = K reversed along channels
+    q = torch.randn(B, HQ, 128, generator=g).half()
+    ctx = torch.tensor([l + 1 for l in lens], dtype=torch.int32)
+    out = L.paged_decode_attention(q.cuda(), kc, vc, table.cuda(), ctx.cuda(), SCALE, max(lens) + 1,
+                                   k_scale=ks, v_scale=vs)
+    for b, l in enumerate(lens):
+        xb = seqs[b].permute(1, 0, 2).unsqueeze(0).numpy()           # [1, H, l+1, 128]
+        kq, kscale = O.quantize_per_token(xb, 8)
+        vq, vscale = O.quantize_per_token(np.ascontiguousarray(xb[..., ::-1]), 8)
+        kd, vd = O.dequant_int8_to_f16(kq, kscale.astype(np.float16), vq, vscale.astype(np.float16))
+        ref = O.decode_attention(q[b:b + 1].numpy(), kd, vd, SCALE)
+        assert_attn_close(out[b:b + 1].cpu().numpy(), ref)
