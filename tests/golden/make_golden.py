@@ -1,7 +1,7 @@
 """Generate the golden vectors that pin the CPU oracle to the reference.
 
-Run in a container where the reference checkout is mounted (default
-``/root/reference``; override with ``LLMIK_REFERENCE``)::
+Run where the reference checkout is available (its location is taken from
+``LLMIK_REFERENCE``, with the build container's mount point as default)::
 
     python tests/golden/make_golden.py
 
