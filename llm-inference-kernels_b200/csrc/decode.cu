@@ -668,6 +668,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
     float m_run = -INFINITY, l_run = 0.f;
     float acc[HB][PVC];
     uint32_t qh[HB][8];  // q * softmax_scale * log2e as half2, in the format's pair order
+    // INT8: K codes enter the dot product as 1152 + code (fp16, exact); this
+    // per-head term, -1152 * (sum of the lane's 16 q values), starts the
+    // lane's partial sum and cancels the offset
+    float kbias[HB];
+#pragma unroll
+    for (int h = 0; h < HB; ++h) kbias[h] = 0.f;
     uint32_t kg[8];      // INT4: K group scale of the lane's 16 channels (pair order)
     uint32_t kgz[8];     // INT4 asym: K group zero
     long long cur_unit = -1, seg_t0 = 0, qoff = 0, bk = 0, seq_len = 0;
@@ -749,6 +755,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
 #pragma unroll
                     for (int c = 0; c < 8; ++c) qh[h][c] = as_u32(__floats2half2_rn(qf[2 * c], qf[2 * c + 1]));
                 }
+                if (FMT == kI8) {
+                    float lo = 0.f, hi = 0.f;
+                    const uint32_t off = 0x64806480u;  // (1152, 1152)
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) fma_h2_2acc(qh[h][c], off, lo, hi);
+                    kbias[h] = -(lo + hi);
+                }
             }
         }
         LIK_TL(tid == 0 && i == tb, 1);
@@ -781,7 +794,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                     const int tt = wt0 + (gq * QG + pl2) * 4 + grp;
                     float part[HB], part2[HB];
 #pragma unroll
-                    for (int h = 0; h < HB; ++h) part[h] = part2[h] = 0.f;
+                    for (int h = 0; h < HB; ++h) {
+                        part[h] = FMT == kI8 ? kbias[h] : 0.f;
+                        part2[h] = 0.f;
+                    }
                     if (tt < ntok) {
                         const uint8_t* row = sK + tt * ROWB;
                         uint32_t kk[8];
@@ -791,13 +807,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                             kk[0] = ka.x; kk[1] = ka.y; kk[2] = ka.z; kk[3] = ka.w;
                             kk[4] = kb.x; kk[5] = kb.y; kk[6] = kb.z; kk[7] = kb.w;
                         } else if (FMT == kI8) {
-                            // raw codes; the token scale multiplies the reduced score
+                            // codes as 1152 + code (offset cancelled by kbias); the
+                            // token scale multiplies the reduced score
                             const uint4 ka = *reinterpret_cast<const uint4*>(row + jl * 16);
-                            half2 a0, a1;
-                            i8x4_to_h2(ka.x, a0, a1); kk[0] = as_u32(a0); kk[1] = as_u32(a1);
-                            i8x4_to_h2(ka.y, a0, a1); kk[2] = as_u32(a0); kk[3] = as_u32(a1);
-                            i8x4_to_h2(ka.z, a0, a1); kk[4] = as_u32(a0); kk[5] = as_u32(a1);
-                            i8x4_to_h2(ka.w, a0, a1); kk[6] = as_u32(a0); kk[7] = as_u32(a1);
+                            i8x4_to_h2_offset(ka.x, kk[0], kk[1]);
+                            i8x4_to_h2_offset(ka.y, kk[2], kk[3]);
+                            i8x4_to_h2_offset(ka.z, kk[4], kk[5]);
+                            i8x4_to_h2_offset(ka.w, kk[6], kk[7]);
                         } else {
                             const int tabs = static_cast<int>(t0) + tt;
                             if (cur_g < 0 || tabs >= gnext) {

@@ -134,6 +134,14 @@ __device__ __forceinline__ void i8x4_to_h2(uint32_t w, half2& lo, half2& hi) {
     hi = __hsub2(as_h2(b), bias);
 }
 
+// Four signed int8 codes -> two half2 holding 1152 + code (exact; the caller
+// removes the offset): (b0, b1), (b2, b3).
+__device__ __forceinline__ void i8x4_to_h2_offset(uint32_t w, uint32_t& lo, uint32_t& hi) {
+    const uint32_t x = w ^ 0x80808080u;
+    lo = __byte_perm(x, 0x64646464u, 0x4140);
+    hi = __byte_perm(x, 0x64646464u, 0x4342);
+}
+
 // Eight packed nibbles (one word: byte i = channel 2i low nibble, 2i+1 high)
 // -> four half2 holding channels (0,4), (1,5), (2,6), (3,7).
 // SIGNED: two's complement nibbles in [-8, 7]; otherwise unsigned 0..15.
