@@ -55,6 +55,7 @@
 #include <algorithm>
 #include <cmath>
 #include <mutex>
+#include <type_traits>
 
 #include "lik_device.cuh"
 #include "lik_internal.h"
@@ -785,7 +786,66 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
             // Passes (4 positions each) are processed QG at a time so that,
             // after the 8-lane reduce-scatter of QG*HB partial sums, every lane
             // holds exactly one distinct (position, head) score.
+            // K group scale (and zero) of group g for the lane's 16 channels
+            auto load_group = [&](int g) {
+                cur_g = g;
+                gnext = (g + 1) * p.group_size;
+                const __half* gsp;
+                const __half* gzp = nullptr;
+                if (p.kg_smem) {
+                    const int g0 = static_cast<int>(t0) / p.group_size;
+                    gsp = reinterpret_cast<const __half*>(sb + p.off_kgs) + (g - g0) * kHeadDim;
+                    if (F::ZK) gzp = reinterpret_cast<const __half*>(sb + p.off_kgz) + (g - g0) * kHeadDim;
+                } else {
+                    long long gb = (bk * p.ng_buf + g) * kHeadDim;
+                    if (p.paged) {
+                        const long long pos = static_cast<long long>(g) * p.group_size;
+                        const long long sq = bk / p.n_kv_heads;
+                        const long long page = p.block_tables[sq * p.max_blocks + pos / p.block_size];
+                        gb = ((page * p.n_kv_heads + (bk - sq * p.n_kv_heads)) *
+                                  (p.block_size / p.group_size) + (pos % p.block_size) / p.group_size) *
+                             kHeadDim;
+                    }
+                    gsp = p.ks + gb;
+                    if (F::ZK) gzp = p.kz + gb;
+                }
+                const uint4 s0 = *reinterpret_cast<const uint4*>(gsp + 16 * jl);
+                const uint4 s1 = *reinterpret_cast<const uint4*>(gsp + 16 * jl + 8);
+                const __half* sh0 = reinterpret_cast<const __half*>(&s0);
+                const __half* sh1 = reinterpret_cast<const __half*>(&s1);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    kg[k] = as_u32(__halves2half2(sh0[k], sh0[k + 4]));
+                    kg[4 + k] = as_u32(__halves2half2(sh1[k], sh1[k + 4]));
+                }
+                if (F::ZK) {
+                    const uint4 z0 = *reinterpret_cast<const uint4*>(gzp + 16 * jl);
+                    const uint4 z1 = *reinterpret_cast<const uint4*>(gzp + 16 * jl + 8);
+                    const __half* zh0 = reinterpret_cast<const __half*>(&z0);
+                    const __half* zh1 = reinterpret_cast<const __half*>(&z1);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        kgz[k] = as_u32(__halves2half2(zh0[k], zh0[k + 4]));
+                        kgz[4 + k] = as_u32(__halves2half2(zh1[k], zh1[k + 4]));
+                    }
+                }
+            };
+            // When the warp's positions of this tile lie in one K group (group
+            // sizes that are multiples of 32), its scales are loaded once here
+            // and the unrolled passes carry no reload code.
+            bool group_checks = false;
+            if constexpr (F::KG) {
+                const int pos_lo = static_cast<int>(t0) + wt0;
+                const int g_lo = pos_lo / p.group_size;
+                if (g_lo == (pos_lo + nval - 1) / p.group_size) {
+                    if (g_lo != cur_g) load_group(g_lo);
+                } else {
+                    group_checks = true;
+                }
+            }
             float sc[NGRP];
+            auto qk_tile = [&](auto check_tag) {
+            constexpr bool CHECK = decltype(check_tag)::value;
 #pragma unroll
             for (int gq = 0; gq < NGRP; ++gq) {
                 float vals[QV];
@@ -816,50 +876,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                             i8x4_to_h2_offset(ka.w, kk[6], kk[7]);
                         } else {
                             const int tabs = static_cast<int>(t0) + tt;
-                            if (cur_g < 0 || tabs >= gnext) {
-                                const int g = tabs / p.group_size;
-                                cur_g = g;
-                                gnext = (g + 1) * p.group_size;
-                                const __half* gsp;
-                                const __half* gzp = nullptr;
-                                if (p.kg_smem) {
-                                    const int g0 = static_cast<int>(t0) / p.group_size;
-                                    gsp = reinterpret_cast<const __half*>(sb + p.off_kgs) + (g - g0) * kHeadDim;
-                                    if (F::ZK) gzp = reinterpret_cast<const __half*>(sb + p.off_kgz) + (g - g0) * kHeadDim;
-                                } else {
-                                    long long gb = (bk * p.ng_buf + g) * kHeadDim;
-                                    if (p.paged) {
-                                        const long long pos = static_cast<long long>(g) * p.group_size;
-                                        const long long sq = bk / p.n_kv_heads;
-                                        const long long page = p.block_tables[sq * p.max_blocks + pos / p.block_size];
-                                        gb = ((page * p.n_kv_heads + (bk - sq * p.n_kv_heads)) *
-                                                  (p.block_size / p.group_size) + (pos % p.block_size) / p.group_size) *
-                                             kHeadDim;
-                                    }
-                                    gsp = p.ks + gb;
-                                    if (F::ZK) gzp = p.kz + gb;
-                                }
-                                const uint4 s0 = *reinterpret_cast<const uint4*>(gsp + 16 * jl);
-                                const uint4 s1 = *reinterpret_cast<const uint4*>(gsp + 16 * jl + 8);
-                                const __half* sh0 = reinterpret_cast<const __half*>(&s0);
-                                const __half* sh1 = reinterpret_cast<const __half*>(&s1);
-    #pragma unroll
-                                for (int k = 0; k < 4; ++k) {
-                                    kg[k] = as_u32(__halves2half2(sh0[k], sh0[k + 4]));
-                                    kg[4 + k] = as_u32(__halves2half2(sh1[k], sh1[k + 4]));
-                                }
-                                if (F::ZK) {
-                                    const uint4 z0 = *reinterpret_cast<const uint4*>(gzp + 16 * jl);
-                                    const uint4 z1 = *reinterpret_cast<const uint4*>(gzp + 16 * jl + 8);
-                                    const __half* zh0 = reinterpret_cast<const __half*>(&z0);
-                                    const __half* zh1 = reinterpret_cast<const __half*>(&z1);
-    #pragma unroll
-                                    for (int k = 0; k < 4; ++k) {
-                                        kgz[k] = as_u32(__halves2half2(zh0[k], zh0[k + 4]));
-                                        kgz[4 + k] = as_u32(__halves2half2(zh1[k], zh1[k + 4]));
-                                    }
-                                }
-                            }
+                            if (CHECK && (cur_g < 0 || tabs >= gnext)) load_group(tabs / p.group_size);
                             const uint2 kw = *reinterpret_cast<const uint2*>(row + jl * 8);
                             half2 c0[4], c1[4];
                             i4x8_to_h2<F::SIGNED>(kw.x, c0);
@@ -892,6 +909,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                 }
                 sc[gq] = s;
             }
+            };
+            if (group_checks)
+                qk_tile(std::true_type{});
+            else
+                qk_tile(std::false_type{});
 
             // ---------------- online softmax (log2 domain) ----------------
             // lanes sharing a head differ in the pass bits (xor 1 .. QG/2) and
