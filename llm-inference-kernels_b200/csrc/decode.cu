@@ -106,7 +106,7 @@ struct DecodeParams {
     int group_size, tok_bulk, kg_smem, ngt;
     int n_ctas, nst, stage_bytes;
     int off_v, off_ks, off_vs, off_vz, off_kgs, off_kgz, off_q;
-    int off_work, off_abuf, off_ml, off_misc, off_bar;
+    int off_work, off_abuf, off_sc, off_ml, off_misc, off_bar;
     float qscale;
     // paged KV (paged != 0): caches are [num_blocks, n_kv_heads, block_size, row],
     // per-token scales [num_blocks, n_kv_heads, block_size], K group scales
@@ -844,9 +844,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                 }
             }
             float sc[NGRP];
+            // INT4: the groups of passes run as a rolled loop (a shorter hot
+            // loop) and park their scores in the warp's shared-memory slots
+            float* scs = reinterpret_cast<float*>(smem + p.off_sc) + w * NGRP * 32;
             auto qk_tile = [&](auto check_tag) {
             constexpr bool CHECK = decltype(check_tag)::value;
-#pragma unroll
+#pragma unroll(F::KG ? 1 : NGRP)
             for (int gq = 0; gq < NGRP; ++gq) {
                 float vals[QV];
 #pragma unroll
@@ -907,7 +910,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                 } else if (F::TOKK) {
                     s *= __half2float(sks[tt]);
                 }
-                sc[gq] = s;
+                if constexpr (F::KG)
+                    scs[gq * 32 + lane] = s;
+                else
+                    sc[gq] = s;
+            }
+            if constexpr (F::KG) {
+#pragma unroll
+                for (int gq = 0; gq < NGRP; ++gq) sc[gq] = scs[gq * 32 + lane];
             }
             };
             if (group_checks)
@@ -1224,7 +1234,11 @@ lik_status launch_t(const DecodeArgs& a, const DeviceInfo& di, cudaStream_t stre
     // per-warp fp16 softmax weights, then the per-warp raw accumulators
     const int pbuf_bytes = static_cast<int>(align_up(static_cast<size_t>(kNCW) * (T / kNCW) * HB * 2, 16));
     const int abuf_bytes = kNCW * HB * kHeadDim * 4;
-    const int work = pbuf_bytes + abuf_bytes;
+    // INT4 formats: per-warp score slots (one float per lane and pass group)
+    constexpr int kNP = T / kNCW / 4;
+    constexpr int kQG = (8 / HB) < kNP ? (8 / HB) : kNP;
+    const int sc_bytes = F::KG ? kNCW * (kNP / kQG) * 32 * 4 : 0;
+    const int work = pbuf_bytes + abuf_bytes + sc_bytes;
     const int fixed = work + kNCW * HB * 3 * 4 + 80 + (3 * 8 + 2) * 8;
     int nst = (di.max_smem_optin - fixed - 256) / p.stage_bytes;
     nst = std::min(nst, 8);
@@ -1237,6 +1251,7 @@ lik_status launch_t(const DecodeArgs& a, const DeviceInfo& di, cudaStream_t stre
     size_t o2 = static_cast<size_t>(nst) * p.stage_bytes;
     p.off_work = static_cast<int>(o2);
     p.off_abuf = static_cast<int>(o2 + pbuf_bytes);
+    p.off_sc = static_cast<int>(o2 + pbuf_bytes + abuf_bytes);
     o2 += work;
     p.off_ml = static_cast<int>(o2);
     o2 += kNCW * HB * 3 * 4;
