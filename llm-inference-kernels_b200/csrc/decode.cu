@@ -849,7 +849,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
             float* scs = reinterpret_cast<float*>(smem + p.off_sc) + w * NGRP * 32;
             auto qk_tile = [&](auto check_tag) {
             constexpr bool CHECK = decltype(check_tag)::value;
-#pragma unroll(F::KG ? 1 : NGRP)
+#pragma unroll(F::KG ? 1 : 16)
             for (int gq = 0; gq < NGRP; ++gq) {
                 float vals[QV];
 #pragma unroll
