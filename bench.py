@@ -79,6 +79,12 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--profile", action="store_true",
                     help="profiler-friendly run: one warm replay, short e2e legs (timings not for reporting)")
+    ap.add_argument("--case", choices=["f16", "int8", "int4", "int4_asym"],
+                    help="profiling case: only `--launches` decode launches of this KV format at the config-1 "
+                         "shape (one copy of the inputs, larger than L2), no timing, no JSON line")
+    ap.add_argument("--launches", type=int, default=3, help="launches of --case")
+    ap.add_argument("--batch", type=int, default=C1["batch"], help="batch of --case")
+    ap.add_argument("--seqlen", type=int, default=C1["seqlen"], help="seqlen of --case")
     return ap.parse_args()
 
 
@@ -621,8 +627,23 @@ def run_ours(args):
     return 0
 
 
+def run_case(args):
+    """A few decode launches of one KV format for ncu captures (small, bounded)."""
+    import torch
+    import llmik_cuda as L
+    dev = torch.device("cuda", 0)
+    wl = Workload(torch, L, dev, args.case, args.batch, args.seqlen, 0, 1)
+    for i in range(args.launches):
+        wl.step(i)
+    torch.cuda.synchronize()
+    print(f"case {args.case}: {args.launches} launches ok", flush=True)
+    return 0
+
+
 def main():
     args = parse()
+    if args.case:
+        return run_case(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

@@ -41,7 +41,7 @@
 extern "C" {
 #endif
 
-#define LLMIK_ABI_VERSION 1
+#define LLMIK_ABI_VERSION 2
 
 typedef enum lik_status {
     LIK_OK = 0,
@@ -50,7 +50,8 @@ typedef enum lik_status {
     LIK_ERR_MISALIGNED = 3,         /* a pointer lacks the 16-byte alignment required */
     LIK_ERR_WORKSPACE = 4,          /* workspace missing or too small */
     LIK_ERR_CUDA = 5,               /* a CUDA runtime call or launch failed */
-    LIK_ERR_DEVICE_TIMEOUT = 6      /* a bounded device-side wait gave up */
+    LIK_ERR_DEVICE_TIMEOUT = 6,     /* a bounded device-side wait gave up */
+    LIK_ERR_DEVICE_BAD_BLOCK = 7    /* a paged block-table entry was outside [0, num_blocks) */
 } lik_status;
 
 /* ---- library information and errors ---------------------------------- */
@@ -71,10 +72,24 @@ size_t lik_decode_workspace_bytes(int64_t batch, int64_t n_heads, int64_t n_kv_h
 lik_status lik_workspace_init(void* workspace, size_t workspace_bytes, void* stream);
 
 /* Read (and clear) the device error word that kernels set when a bounded
- * device-side wait expires. Synchronizes `stream`. *device_error = 0 means no
- * error. */
+ * device-side wait expires (*device_error = 1, LIK_ERR_DEVICE_TIMEOUT) or a
+ * paged block-table entry is out of range (2, LIK_ERR_DEVICE_BAD_BLOCK).
+ * Synchronizes `stream`. *device_error = 0 means no error. After an error the
+ * whole workspace is zeroed again on `stream` (a kernel that gave up may have
+ * left unit counters behind), so it can be reused as is. */
 lik_status lik_workspace_check(void* workspace, size_t workspace_bytes, void* stream,
                                int* device_error);
+
+/* Failure-detection self test of the recovery path (no reference
+ * counterpart): a one-warp kernel runs the decode kernels' bounded wait
+ * (`polls` polls) on a barrier nothing arrives at and, when it gives up,
+ * leaves what a decode kernel that gave up leaves: the timeout code in the
+ * error word and a non-zero unit counter. Target: `workspace` (a zeroed decode
+ * workspace of `workspace_bytes`), or, when workspace is NULL, the fixed
+ * scratch of lik_decode_attention_f16_noalloc on the current device. The
+ * next lik_workspace_check / lik_decode_noalloc_check must report the error
+ * and reset the scratch. Asynchronous on `stream`. */
+lik_status lik_selftest_leave_timeout(int64_t polls, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Failure-detection self test (no reference counterpart): runs a one-warp
  * kernel that waits, with the decode kernels' bounded poll loop limited to
@@ -102,17 +117,28 @@ lik_status lik_decode_attention_f16(
  * holds the raw pointers it was given). No counterpart in the reference.
  * Same arguments and results as lik_decode_attention_f16 minus the
  * workspace. Its scratch is a fixed 4 MiB array inside the library that every
- * GPU loading the library keeps until exit; shapes whose
- * lik_decode_workspace_bytes() exceeds 4 MiB are rejected with
+ * GPU loading the library keeps until exit (zero when the library loads);
+ * shapes whose lik_decode_workspace_bytes() exceeds 4 MiB are rejected with
  * LIK_ERR_WORKSPACE. The first call on each device looks up that array's
- * device address and zeroes it (synchronously), so make that first call
+ * device address (a host-side query, no device work), so make that first call
  * before any stream capture. All calls on a device share the one array:
  * calls that can overlap on the GPU (other streams, other host threads) race
- * and give wrong results; serialize them. */
+ * and give wrong results; serialize them. A bounded device-side wait that
+ * expires inside this path leaves its code in the array's error word; read and
+ * clear it with lik_decode_noalloc_check. */
 lik_status lik_decode_attention_f16_noalloc(
     const void* q, const void* k, const void* v, void* out,
     int64_t batch, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim,
     int64_t seqlen, int64_t kv_buf_len, float softmax_scale, void* stream);
+
+/* Error check of the allocation-free path (no counterpart in the reference):
+ * reads the device error word of lik_decode_attention_f16_noalloc's fixed
+ * scratch on the current device after the work queued on `stream`
+ * (synchronizes `stream`), like lik_workspace_check does for a caller-owned
+ * workspace: *device_error = 0 and LIK_OK when clean; otherwise the code
+ * (1 = a bounded wait expired), LIK_ERR_DEVICE_TIMEOUT, and the whole scratch
+ * is zeroed again on `stream` so that later calls start from a clean state. */
+lik_status lik_decode_noalloc_check(void* stream, int* device_error);
 
 /* INT8 per-token KV: K = k_q * k_scale[token], V = v_q * v_scale[token].
  * Replaces launch_decode_attention_int8
@@ -161,13 +187,17 @@ lik_status lik_decode_attention_int4_asym(
  * [0, max_context_len]; each must be >= 1); position t lives at row t %
  * block_size of block block_tables[b][t / block_size]. block_size is a
  * multiple of 16 (and of group_size for INT4); scale/zero pointers are
- * 16-byte aligned. Same workspace rules as the contiguous entry points. */
+ * 16-byte aligned. num_blocks is the number of blocks in the caches: a table
+ * entry a sequence reaches that lies outside [0, num_blocks) is never read
+ * through; its tile is masked and the workspace error word records
+ * LIK_ERR_DEVICE_BAD_BLOCK (lik_workspace_check). Same workspace rules as the
+ * contiguous entry points. */
 lik_status lik_decode_attention_paged(
     int kv_format, const void* q, const void* k_cache, const void* v_cache,
     const void* k_scale, const void* v_scale, const void* k_zero, const void* v_zero,
     const int32_t* block_tables, const int32_t* context_lens, void* out,
     int64_t batch, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim,
-    int64_t block_size, int64_t max_blocks_per_seq, int64_t max_context_len,
+    int64_t num_blocks, int64_t block_size, int64_t max_blocks_per_seq, int64_t max_context_len,
     int64_t group_size, float softmax_scale,
     void* workspace, size_t workspace_bytes, void* stream);
 

@@ -6,6 +6,7 @@
 #include <mutex>
 #include <string>
 
+#include "lik_device.cuh"
 #include "lik_internal.h"
 #include "llmik.h"
 
@@ -89,6 +90,30 @@ lik_status run_decode(DecodeArgs& a, void* stream) {
     return LIK_OK;
 }
 
+}  // namespace
+
+namespace lik {
+
+// Read the device error word at the start of a decode scratch area after the
+// work queued on `stream`; on an error, zero the whole area on `stream` (a
+// kernel that gave up may have left unit counters behind) and report it.
+lik_status check_error_word(void* scratch, size_t scratch_bytes, cudaStream_t stream, int* device_error) {
+    int h = 0;
+    cudaError_t e = cudaMemcpyAsync(&h, scratch, sizeof(int), cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    if (e == cudaSuccess && h != 0) e = cudaMemsetAsync(scratch, 0, scratch_bytes, stream);
+    if (e != cudaSuccess) return fail(LIK_ERR_CUDA, std::string("error-word check: ") + cudaGetErrorString(e));
+    *device_error = h;
+    if (h == kDevOk) return LIK_OK;
+    if (h == kDevBadBlock)
+        return fail(LIK_ERR_DEVICE_BAD_BLOCK, "a paged block-table entry was outside [0, num_blocks)");
+    return fail(LIK_ERR_DEVICE_TIMEOUT, "a bounded device-side wait expired");
+}
+
+}  // namespace lik
+
+namespace {
+
 lik_status check_quant(const void* x, const void* codes, const void* scale, int64_t batch, int64_t n_kv_heads,
                        int64_t n_tokens, int64_t head_dim, int64_t dst_pos, int64_t dst_buf_len) {
     if (batch < 0 || n_kv_heads <= 0 || n_tokens < 0)
@@ -118,6 +143,7 @@ const char* lik_status_string(lik_status s) {
         case LIK_ERR_WORKSPACE: return "workspace missing or too small";
         case LIK_ERR_CUDA: return "CUDA error";
         case LIK_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
+        case LIK_ERR_DEVICE_BAD_BLOCK: return "block-table entry out of range";
     }
     return "unknown status";
 }
@@ -143,13 +169,7 @@ lik_status lik_workspace_init(void* workspace, size_t workspace_bytes, void* str
 lik_status lik_workspace_check(void* workspace, size_t workspace_bytes, void* stream, int* device_error) {
     if (!workspace || workspace_bytes < kWsErrBytes || !device_error)
         return fail(LIK_ERR_INVALID_ARGUMENT, "workspace and device_error must be given");
-    int h = 0;
-    cudaError_t e = cudaMemcpyAsync(&h, workspace, sizeof(int), cudaMemcpyDeviceToHost, as_stream(stream));
-    if (e == cudaSuccess) e = cudaStreamSynchronize(as_stream(stream));
-    if (e == cudaSuccess && h != 0) e = cudaMemsetAsync(workspace, 0, sizeof(int), as_stream(stream));
-    if (e != cudaSuccess) return fail(LIK_ERR_CUDA, std::string("workspace check: ") + cudaGetErrorString(e));
-    *device_error = h;
-    return h == 0 ? LIK_OK : fail(LIK_ERR_DEVICE_TIMEOUT, "a bounded device-side wait expired");
+    return check_error_word(workspace, workspace_bytes, as_stream(stream), device_error);
 }
 
 lik_status lik_decode_attention_f16(const void* q, const void* k, const void* v, void* out, int64_t batch,
@@ -376,7 +396,8 @@ lik_status lik_decode_attention_paged(int kv_format, const void* q, const void* 
                                       const void* k_scale, const void* v_scale, const void* k_zero, const void* v_zero,
                                       const int32_t* block_tables, const int32_t* context_lens, void* out,
                                       int64_t batch, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim,
-                                      int64_t block_size, int64_t max_blocks_per_seq, int64_t max_context_len,
+                                      int64_t num_blocks, int64_t block_size, int64_t max_blocks_per_seq,
+                                      int64_t max_context_len,
                                       int64_t group_size, float softmax_scale, void* workspace,
                                       size_t workspace_bytes, void* stream) {
     lik_status s = check_heads(batch, n_heads, n_kv_heads, head_dim);
@@ -384,6 +405,7 @@ lik_status lik_decode_attention_paged(int kv_format, const void* q, const void* 
     if (kv_format < kF16 || kv_format > kI4Asym) return fail(LIK_ERR_INVALID_ARGUMENT, "unknown kv_format");
     if (block_size <= 0 || block_size % 16 != 0 || block_size > (1 << 20))
         return fail(LIK_ERR_INVALID_ARGUMENT, "block_size must be a positive multiple of 16");
+    if (num_blocks < 1) return fail(LIK_ERR_INVALID_ARGUMENT, "num_blocks must be >= 1");
     if (max_blocks_per_seq <= 0 || max_context_len < 1 || max_context_len > block_size * max_blocks_per_seq ||
         max_context_len > (int64_t{1} << 30))
         return fail(LIK_ERR_INVALID_ARGUMENT, "need 1 <= max_context_len <= block_size * max_blocks_per_seq");
@@ -407,7 +429,7 @@ lik_status lik_decode_attention_paged(int kv_format, const void* q, const void* 
     a.group_size = int4 ? group_size : 0;
     a.n_groups_buf = int4 ? (max_context_len + group_size - 1) / group_size : 0;
     a.block_tables = block_tables; a.context_lens = context_lens;
-    a.block_size = block_size; a.max_blocks = max_blocks_per_seq;
+    a.block_size = block_size; a.max_blocks = max_blocks_per_seq; a.num_blocks = num_blocks;
     a.softmax_scale = softmax_scale;
     a.workspace = workspace; a.workspace_bytes = workspace_bytes;
     return run_decode(a, stream);

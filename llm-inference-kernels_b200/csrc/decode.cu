@@ -65,7 +65,12 @@ namespace lik {
 constexpr int kNCW = 8;                    // consumer warps
 constexpr int kProducerWarp = kNCW;      // issues the bulk copies
 constexpr int kEpilogueWarp = kNCW + 1;  // finishes unit segments off the streaming path
+constexpr int kScaleWarp = kNCW + 2;     // tensor-pipe INT4 path: folds K group scales into q
 constexpr int kThreads = (kNCW + 2) * 32;
+template <int FMT, bool MMA>
+constexpr int threads_for() {
+    return (MMA && (FMT == kI4Sym || FMT == kI4Asym)) ? (kNCW + 3) * 32 : kThreads;
+}
 constexpr float kLog2e = 1.4426950408889634f;
 
 template <int FMT>
@@ -91,6 +96,27 @@ struct Fmt<kI4Asym> {
     static constexpr bool TOKK = false, TOKV = true, ZV = true, KG = true, ZK = true, SIGNED = false;
 };
 
+// Division by a launch constant with one multiply-high (dividends and
+// divisors below 2^31; the host rejects launches beyond that):
+// q = (umulhi(x, m) + x) >> s with s = ceil(log2 d), m = 2^32 (2^s - d) / d + 1.
+// Keeps 64-bit integer division (an inlined ~80-instruction sequence per
+// site) out of the streaming loops.
+struct FDiv {
+    uint32_t d, m, s;
+    __device__ __forceinline__ long long q(long long x) const {
+        const uint32_t xx = static_cast<uint32_t>(x);
+        return static_cast<long long>((__umulhi(xx, m) + xx) >> s);
+    }
+    __device__ __forceinline__ long long r(long long x) const { return x - q(x) * static_cast<long long>(d); }
+};
+
+inline FDiv make_fdiv(uint32_t d) {
+    FDiv f{d, 0u, 0u};
+    while ((uint64_t{1} << f.s) < d) ++f.s;
+    f.m = static_cast<uint32_t>(((uint64_t{1} << 32) * ((uint64_t{1} << f.s) - d)) / d + 1);
+    return f;
+}
+
 struct DecodeParams {
     const __half* q;
     __half* out;
@@ -107,6 +133,7 @@ struct DecodeParams {
     int n_ctas, nst, stage_bytes;
     int off_v, off_ks, off_vs, off_vz, off_kgs, off_kgz, off_q;
     int off_work, off_abuf, off_sc, off_ml, off_misc, off_bar;
+    int off_w, off_zk, ngw;  // tensor-pipe INT4 path: per-stage folded K weights, group constants, groups
     float qscale;
     // paged KV (paged != 0): caches are [num_blocks, n_kv_heads, block_size, row],
     // per-token scales [num_blocks, n_kv_heads, block_size], K group scales
@@ -114,10 +141,12 @@ struct DecodeParams {
     // position t lives in block block_tables[b * max_blocks + t / block_size].
     const int* block_tables;
     const int* ctx_lens;
-    int paged, block_size, max_blocks;
+    long long num_blocks;  // pages in the cache; table entries outside [0, num_blocks) are rejected
+    int paged, block_size, max_blocks, off_ntok;
     float* part;
     unsigned* counters;
     int* err;
+    FDiv fd_tpu, fd_nhb, fd_hkv, fd_gs, fd_bs, fd_nst;
 };
 
 // ---- small helpers --------------------------------------------------------
@@ -166,6 +195,17 @@ __device__ __forceinline__ float reduce_scatter8(float (&v)[HB], int lane) {
         }
     }
     return a[0];
+}
+
+// A block-table entry used for a direct global read: out-of-range entries
+// record kDevBadBlock and read page 0 instead (the tile they belong to is
+// masked by the producer).
+__device__ __forceinline__ long long checked_page(const DecodeParams& p, long long page) {
+    if (page < 0 || page >= p.num_blocks) {
+        atomicExch(p.err, kDevBadBlock);
+        return 0;
+    }
+    return page;
 }
 
 __device__ __forceinline__ long long owner_cta(long long tile, long long total, int nctas) {
@@ -356,33 +396,374 @@ __device__ __forceinline__ float h2_sum(half2 a) {
     return f.x + f.y;
 }
 
-// ---- optional timeline probes (diagnostic builds only: -DLIK_TIMELINE) ------
-#ifdef LIK_TIMELINE
-__device__ unsigned long long g_lik_timeline[4096 * 12];
-__device__ __forceinline__ void lik_tl(int slot) {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    g_lik_timeline[blockIdx.x * 12 + slot] = t;
-    if (slot == 0) {
-        unsigned sm;
-        asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));
-        g_lik_timeline[blockIdx.x * 12 + 8] = sm;
+
+// The consumer warps' side of a unit segment's end, once every warp has
+// stored its raw state (m, l per head in mlb; standard accumulators in abuf).
+// Not the CTA's last segment: hand it to the epilogue warp and go on
+// streaming. The CTA's last segment: combine the warp states here (all
+// consumer warps), then write the unit's output or publish the partial, take
+// the unit's ticket and merge the unit if this segment completes it.
+// The CTA's last segment, finished by all consumer warps together.
+template <int HB>
+__device__ __forceinline__ void finish_final_segment(const DecodeParams& p, bool whole, long long unit, long long qoff,
+                                                  long long slot, volatile int* misc, const float* mlb,
+                                                  const float* abuf, const UnitSpan* last_span, int lane, int tid) {
+    constexpr int nct = kNCW * 32;
+    named_bar_sync(1, nct);  // every warp's state is in shared memory
+    WarpCombine<HB> wc;
+    wc.load(mlb, lane);
+    if (whole) {
+        for (int o = tid; o < HB * kHeadDim; o += nct)
+            p.out[qoff + o] = __float2half_rn(wc.combined(abuf, o) / pick<HB>(wc.L, o >> 7));
+    } else {
+        float* sp = p.part + slot * (HB * kHeadDim + 2 * HB);
+        for (int o = tid; o < HB * kHeadDim; o += nct) sp[o] = wc.combined(abuf, o);
+        if (tid < HB) {
+            sp[HB * kHeadDim + tid] = pick<HB>(wc.M, tid);
+            sp[HB * kHeadDim + HB + tid] = pick<HB>(wc.L, tid);
+        }
+        named_bar_sync(1, nct);  // the whole partial is written
+        if (tid == 0) misc[1] = unit_ticket(p, unit, *last_span) ? 1 : 0;
+        named_bar_sync(1, nct);
+        if (misc[1]) merge_segments<HB>(p, *last_span, qoff, tid, nct);
     }
 }
-#define LIK_TL(cond, slot) \
-    do {                   \
-        if (cond) lik_tl(slot); \
-    } while (0)
-#else
-#define LIK_TL(cond, slot) \
-    do {                   \
-    } while (0)
-#endif
+
+// The consumer warps' side of a unit segment's end, once every warp has
+// stored its raw state (m, l per head in mlb; standard accumulators in abuf).
+// Not the CTA's last segment: hand it to the epilogue warp and go on
+// streaming. The CTA's last segment: combine the warp states here (all
+// consumer warps), then write the unit's output or publish the partial, take
+// the unit's ticket and merge the unit if this segment completes it.
+template <int HB>
+__device__ __forceinline__ void finish_segment(const DecodeParams& p, bool final_seg, bool whole, long long unit,
+                                               long long qoff, long long slot, long long& nhand, EpiDesc* desc,
+                                               uint64_t* epi_full, volatile int* misc, const float* mlb,
+                                               const float* abuf, const UnitSpan* last_span, int w, int lane,
+                                               int tid) {
+    if (!final_seg) {
+        if (w == 0 && lane == 0) {
+            EpiDesc d;
+            d.unit = unit;
+            d.qoff = qoff;
+            d.slot = slot;
+            d.whole = whole ? 1 : 0;
+            d.pad = 0;
+            *desc = d;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(epi_full);  // release: the state and descriptor
+        ++nhand;
+        return;
+    }
+    finish_final_segment<HB>(p, whole, unit, qoff, slot, misc, mlb, abuf, last_span, lane, tid);
+}
+
+// One segment hand-off processed by the epilogue warp.
+template <int HB>
+__device__ __forceinline__ void epilogue_handoff(const DecodeParams& p, const EpiDesc& d, const float* mlb,
+                                              const float* abuf, uint64_t* epi_empty, int lane) {
+    constexpr int HBK = HB * kHeadDim;
+    WarpCombine<HB> wc;
+    wc.load(mlb, lane);
+    if (d.whole) {
+        for (int o = lane; o < HBK; o += 32)
+            p.out[d.qoff + o] = __float2half_rn(wc.combined(abuf, o) / pick<HB>(wc.L, o >> 7));
+        __syncwarp();
+        if (lane == 0) mbar_arrive(epi_empty);
+    } else {
+        float* sp = p.part + d.slot * (HBK + 2 * HB);
+        for (int o = lane; o < HBK; o += 32) sp[o] = wc.combined(abuf, o);
+        if (lane < HB) {
+            sp[HBK + lane] = pick<HB>(wc.M, lane);
+            sp[HBK + HB + lane] = pick<HB>(wc.L, lane);
+        }
+        __syncwarp();  // the partial is written; the shared state is free again
+        if (lane == 0) mbar_arrive(epi_empty);
+        const UnitSpan span = unit_span(p, d.unit);
+        int last = 0;
+        if (lane == 0) last = unit_ticket(p, d.unit, span);
+        last = __shfl_sync(kFull, last, 0);
+        if (last) merge_segments<HB>(p, span, d.qoff, lane, 32);
+    }
+}
+
+// Before a consumer warp overwrites the shared hand-off state: the epilogue
+// warp has read the previous hand-off (bounded wait).
+__device__ __forceinline__ void wait_handoff_free(const DecodeParams& p, uint64_t* epi_empty, volatile int* misc,
+                                                  long long nhand, int lane) {
+    if (lane == 0 && nhand > 0 && !mbar_wait_bounded(epi_empty, static_cast<uint32_t>((nhand - 1) & 1))) {
+        misc[0] = 1;
+        atomicExch(p.err, kDevWaitTimeout);
+    }
+    __syncwarp();
+}
+
+
+// Reduce each of the N (a power of two <= 32) values over the 32 lanes of the
+// warp with OP (sum or max), scattering them: afterwards lane l holds the
+// full result for value `head` (the same for the 32 / N lanes that share the
+// bits above log2(32 / N)). log2(N) halving exchanges plus log2(32 / N)
+// butterfly steps: N - 1 + 5 - log2(N) shuffles instead of 5 N.
+struct OpSum {
+    template <typename T>
+    __device__ __forceinline__ T operator()(T a, T b) const { return a + b; }
+};
+struct OpMax {
+    __device__ __forceinline__ float operator()(float a, float b) const { return fmaxf(a, b); }
+};
+template <int N, typename T, typename OP>
+__device__ __forceinline__ T lane_reduce_scatter(T (&v)[N], int lane, int& head, OP op) {
+    int n = N, h = 0, b = 4;
+#pragma unroll
+    for (int step = 0; step < 5; ++step, --b) {
+        if (n > 1) {
+            const int half = n >> 1;
+            const bool up = (lane >> b) & 1;
+#pragma unroll
+            for (int i = 0; i < N / 2; ++i) {
+                if (i < half) {
+                    const T send = up ? v[i] : v[i + half];
+                    const T keep = up ? v[i + half] : v[i];
+                    v[i] = op(keep, __shfl_xor_sync(kFull, send, 1 << b));
+                }
+            }
+            if (up) h += half;
+            n = half;
+        } else {
+            v[0] = op(v[0], __shfl_xor_sync(kFull, v[0], 1 << b));
+        }
+    }
+    head = h;
+    return v[0];
+}
+template <int N>
+__device__ __forceinline__ constexpr int lane_of_result(int h) {
+    return h * (32 / N);
+}
+
+// ---- tensor-pipe building blocks (INT8 / INT4 formats) --------------------
+//
+// QK and PV run as mma.sync m16n8k16 (f16 x f16 -> f32). Codes enter the
+// tensor pipe as fp16 *subnormals*: a nibble or byte n masked into the low
+// mantissa bits of a half is exactly n * 2^-24 (a nibble masked at bits 4..7 is
+// 16 n * 2^-24), one LOP3 per two values and no conversion; the tensor pipe
+// multiplies subnormal inputs exactly (checked on B200: no flush to zero).
+// Scales and zeros never touch the codes: per-channel K group scales are folded
+// into q (w_c = q_c * scale_c, fp16), per-token scales into the score (INT8 K)
+// or into the softmax weight (p' = p * v_scale, fp16), and the zero points /
+// code offsets become per-head constants added in fp32:
+//   INT4 asym K : s = 2^24 * sum_c w_c n_c            + sum_c q_c z_c
+//   INT4 sym  K : s = 2^24 * sum_c w_c (c_c + 8)      - 8 sum_c w_c
+//   INT8      K : s = k_scale * (2^24 * sum_c w_c (c_c + 128) - 128 sum_c w_c)
+//   V           : o = 2^24 * sum_t p'_t u_t + (sum_t p_t z_t  |  -off * sum_t p'_t)
+// where u is the fed code (n, c + 8 or c + 128) and the offset sums use the
+// fp16 weights actually fed to the MMA, so the offsets cancel exactly.
+//
+// Fragment maps (g = lane / 4, r = lane % 4; rho swaps bits 0 and 1 of a row
+// index, which spreads the V rows one instruction reads over both halves of
+// the shared-memory banks):
+//   QK  A = K tile (16 positions x 16 channels): lane rows rho(g), rho(g) + 8;
+//       channels: lane r's block of 32 (INT4: bytes 16r..16r+15 of a row,
+//       INT8: bytes 32r..32r+31), in the order the masks extract them.
+//       B = folded q (16 channels x 8 heads), lane column = head g.
+//       D = scores (positions x heads): lane holds heads 2r, 2r+1.
+//   PV  A = V^T (16 channels x 16 positions), B = p'^T (positions x heads),
+//       obtained from the QK accumulator layout by movmatrix.trans.
+//       D = output^T: lane holds channels 16g + 2mt (+1) of heads 2r, 2r+1.
+
+__device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                              uint32_t b0, uint32_t b1) {
+    asm(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+    uint32_t y;
+    asm("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+    return as_u32(__floats2half2_rn(lo, hi));
+}
+
+// rho: the row permutation of a 16-row MMA tile (swap bits 0 and 1)
+__device__ __forceinline__ int rho(int i) { return (i & ~3) | ((i & 1) << 1) | ((i & 2) >> 1); }
+
+template <int FMT>
+struct MmaFmt {
+    // nibble formats: codes as 4-bit fields; XOR turns two's complement into
+    // offset binary (c + 8) for the symmetric format
+    static constexpr bool I4 = FMT == kI4Sym || FMT == kI4Asym;
+    static constexpr uint32_t X4 = FMT == kI4Sym ? 0x88888888u : 0u;
+    static constexpr float VOFF = FMT == kI4Sym ? 8.f : FMT == kI8 ? 128.f : 0.f;  // V code offset
+    // fixed-point limbs of the folded QK weights (INT8: 16 bits, INT4: 24 bits;
+    // the INT4 weights carry the K group scale and need the wider range)
+    static constexpr int L = I4 ? 3 : 2;
+    // Softmax weights may reach 2^kTau before the running maximum is raised.
+    // The fp16 weight p * v_scale stays finite for every fp16 V: v_scale is at
+    // most 65504 / 127 (INT8) or 2 * 65504 / 15 (INT4), so p <= 64 resp. 4.
+    static constexpr float kTau = FMT == kI8 ? 6.f : 2.f;
+};
+
+// two subnormal halves from the low (x & 0x000F000F) / high (x & 0x00F000F0)
+// nibble of each 16-bit half of x (after the format's XOR)
+template <int FMT>
+__device__ __forceinline__ uint32_t nib_lo(uint32_t x) {
+    return (x ^ MmaFmt<FMT>::X4) & 0x000F000Fu;
+}
+template <int FMT>
+__device__ __forceinline__ uint32_t nib_hi(uint32_t x) {
+    return (x ^ MmaFmt<FMT>::X4) & 0x00F000F0u;
+}
+// two subnormal halves from bytes 0 and 2 of x, two's complement -> c + 128
+__device__ __forceinline__ uint32_t byte_pair(uint32_t x) { return (x ^ 0x00800080u) & 0x00FF00FFu; }
+
+// Integer MMA m16n8k32 (s32 accumulate): A = K codes as bytes (s8 for INT8,
+// u8 nibble values for INT4), B = one 8-bit limb of the folded q weights
+// (the top limb signed, lower limbs unsigned).
+template <bool AU, bool BU>
+__device__ __forceinline__ void mma_i8_16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+    if constexpr (AU && BU)
+        asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+            : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    else if constexpr (AU && !BU)
+        asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+            : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    else if constexpr (!AU && BU)
+        asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+            : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    else
+        asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+            : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// QK of one 16-position m-tile on the integer tensor pipe. K rows at krow
+// (the lane's row rho(g); the second row is 8 rows further), the lane's
+// 32-channel block r already offset. The folded weights are fixed point with
+// L 8-bit limbs per head: B[l][ks][0..1] is the B fragment of limb l (0 = top)
+// at k-step ks. d[l] receives sum_c code_c * limb_l(w_c).
+//   INT8: the 32 code bytes of a row are the A fragments as loaded (k-step ks
+//         uses words 2ks, 2ks+1: channels 32r + 8ks + 0..7).
+//   INT4: word j of a row holds channels 32r + 8j + 0..7 as nibbles;
+//         (w & 0x0F0F0F0F) gives the even channels and (w >> 4) & 0x0F0F0F0F
+//         the odd ones as bytes (the symmetric format XORs 8 first: c + 8).
+template <int FMT, int L>
+__device__ __forceinline__ void qk_mtile_int(const uint8_t* krow, const uint32_t (&B)[L][4][2], int (&d)[L][4]) {
+#pragma unroll
+    for (int l = 0; l < L; ++l)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) d[l][c] = 0;
+    if constexpr (MmaFmt<FMT>::I4) {
+        constexpr uint32_t X = FMT == kI4Sym ? 0x08080808u : 0u;
+        const uint4 k0 = *reinterpret_cast<const uint4*>(krow);
+        const uint4 k1 = *reinterpret_cast<const uint4*>(krow + 8 * 64);
+        const uint32_t w0[4] = {k0.x, k0.y, k0.z, k0.w};
+        const uint32_t w1[4] = {k1.x, k1.y, k1.z, k1.w};
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+            const uint32_t e0 = (w0[ks] ^ X) & 0x0F0F0F0Fu, e1 = (w1[ks] ^ X) & 0x0F0F0F0Fu;
+            const uint32_t o0 = ((w0[ks] >> 4) ^ X) & 0x0F0F0F0Fu, o1 = ((w1[ks] >> 4) ^ X) & 0x0F0F0F0Fu;
+#pragma unroll
+            for (int l = 0; l < L; ++l) {
+                if (l == 0)
+                    mma_i8_16832<true, false>(d[l], e0, e1, o0, o1, B[l][ks][0], B[l][ks][1]);
+                else
+                    mma_i8_16832<true, true>(d[l], e0, e1, o0, o1, B[l][ks][0], B[l][ks][1]);
+            }
+        }
+    } else {
+        const uint4 k0a = *reinterpret_cast<const uint4*>(krow);
+        const uint4 k0b = *reinterpret_cast<const uint4*>(krow + 16);
+        const uint4 k1a = *reinterpret_cast<const uint4*>(krow + 8 * 128);
+        const uint4 k1b = *reinterpret_cast<const uint4*>(krow + 8 * 128 + 16);
+        const uint32_t w0[8] = {k0a.x, k0a.y, k0a.z, k0a.w, k0b.x, k0b.y, k0b.z, k0b.w};
+        const uint32_t w1[8] = {k1a.x, k1a.y, k1a.z, k1a.w, k1b.x, k1b.y, k1b.z, k1b.w};
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+#pragma unroll
+            for (int l = 0; l < L; ++l) {
+                if (l == 0)
+                    mma_i8_16832<false, false>(d[l], w0[2 * ks], w1[2 * ks], w0[2 * ks + 1], w1[2 * ks + 1],
+                                               B[l][ks][0], B[l][ks][1]);
+                else
+                    mma_i8_16832<false, true>(d[l], w0[2 * ks], w1[2 * ks], w0[2 * ks + 1], w1[2 * ks + 1],
+                                              B[l][ks][0], B[l][ks][1]);
+            }
+    }
+}
+
+// The fp16 in half `hf` (0: low, 1: high) of a packed word, as float.
+__device__ __forceinline__ float half_of(uint32_t w, int hf) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(w >> (16 * hf))));
+}
+
+// Pack byte `shift` of four 32-bit values into one register (value i ->
+// byte i).
+__device__ __forceinline__ uint32_t pack_bytes(int v0, int v1, int v2, int v3, int shift) {
+    const uint32_t lo = __byte_perm(static_cast<uint32_t>(v0) >> shift, static_cast<uint32_t>(v1) >> shift, 0x0040);
+    const uint32_t hi = __byte_perm(static_cast<uint32_t>(v2) >> shift, static_cast<uint32_t>(v3) >> shift, 0x0040);
+    return __byte_perm(lo, hi, 0x5410);
+}
+
+// PV of one 16-position k-step: V rows A = vrow, B = A + 2, C = A + 8,
+// D = A + 10 (positions rho(2r), rho(2r+1), rho(2r) + 8, rho(2r+1) + 8), the
+// lane's 16 channels starting at byte vcol; (b0, b1) = p'^T fragment.
+template <int FMT>
+__device__ __forceinline__ void pv_kstep(const uint8_t* vrow, uint32_t b0, uint32_t b1, float (&acc)[8][4]) {
+    if constexpr (MmaFmt<FMT>::I4) {
+        constexpr int RB = 64;
+        const uint2 A = *reinterpret_cast<const uint2*>(vrow);
+        const uint2 B = *reinterpret_cast<const uint2*>(vrow + 2 * RB);
+        const uint2 C = *reinterpret_cast<const uint2*>(vrow + 8 * RB);
+        const uint2 D = *reinterpret_cast<const uint2*>(vrow + 10 * RB);
+        const uint32_t a[2] = {A.x, A.y}, b[2] = {B.x, B.y}, c[2] = {C.x, C.y}, dd[2] = {D.x, D.y};
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const uint32_t ab[2] = {__byte_perm(a[j], b[j], 0x5410), __byte_perm(a[j], b[j], 0x7632)};
+            const uint32_t cd[2] = {__byte_perm(c[j], dd[j], 0x5410), __byte_perm(c[j], dd[j], 0x7632)};
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                const uint32_t xa = ab[t >> 1] >> ((t & 1) * 8);
+                const uint32_t xc = cd[t >> 1] >> ((t & 1) * 8);
+                mma_f16_16816(acc[4 * j + t], nib_lo<FMT>(xa), nib_hi<FMT>(xa), nib_lo<FMT>(xc), nib_hi<FMT>(xc), b0,
+                              b1);
+            }
+        }
+    } else {
+        constexpr int RB = 128;
+        const uint4 A = *reinterpret_cast<const uint4*>(vrow);
+        const uint4 B = *reinterpret_cast<const uint4*>(vrow + 2 * RB);
+        const uint4 C = *reinterpret_cast<const uint4*>(vrow + 8 * RB);
+        const uint4 D = *reinterpret_cast<const uint4*>(vrow + 10 * RB);
+        const uint32_t a[4] = {A.x, A.y, A.z, A.w}, b[4] = {B.x, B.y, B.z, B.w};
+        const uint32_t c[4] = {C.x, C.y, C.z, C.w}, dd[4] = {D.x, D.y, D.z, D.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+                const uint32_t xa = __byte_perm(a[j], b[j], t ? 0x7632 : 0x5410);
+                const uint32_t xc = __byte_perm(c[j], dd[j], t ? 0x7632 : 0x5410);
+                mma_f16_16816(acc[2 * j + t], byte_pair(xa), byte_pair(xa >> 8), byte_pair(xc), byte_pair(xc >> 8),
+                              b0, b1);
+            }
+        }
+    }
+}
 
 // ---- the kernel -----------------------------------------------------------
 
-template <int FMT, int HB>
-__global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams p) {
+template <int FMT, int HB, bool MMA>
+__global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(const DecodeParams p) {
     using F = Fmt<FMT>;
     constexpr int T = F::T;
     constexpr int ROWB = F::ROWB;
@@ -404,6 +785,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
     // warps wrote their state) and "epi_empty" (the epilogue warp has read it)
     uint64_t* epi_full = empty + p.nst;
     uint64_t* epi_empty = epi_full + 1;
+    // tensor-pipe INT4 path: "wfull" (the scale warp wrote the stage's folded weights)
+    uint64_t* wfull = epi_empty + 1;
     volatile int* misc = reinterpret_cast<volatile int*>(smem + p.off_misc);
     EpiDesc* desc = reinterpret_cast<EpiDesc*>(smem + p.off_misc + 16);
     float* abuf = reinterpret_cast<float*>(smem + p.off_abuf);
@@ -421,6 +804,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
         }
         mbar_init(epi_full, kNCW);
         mbar_init(epi_empty, 1);
+        if (MMA && F::KG)
+            for (int s2 = 0; s2 < p.nst; ++s2) mbar_init(&wfull[s2], 1);
         misc[0] = 0;  // abort
         misc[1] = 0;  // merge ticket result
         fence_barrier_init();
@@ -430,7 +815,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
     // read or written before that kernel has completed.
     grid_dependency_wait();
     __syncthreads();
-    LIK_TL(tid == 0, 0);
 
     // ======================= producer warp ================================
     if (warp == kProducerWarp) {
@@ -440,9 +824,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
         // incremental (stage, phase) and (unit, tile) counters: no divisions in the loop
         int st = 0;
         uint32_t ph = 0;
-        long long unit = tb / p.tpu;
+        long long unit = p.fd_tpu.q(tb);
         long long ti = tb - unit * p.tpu;
-        long long bk = unit / p.nhb;
+        long long bk = p.fd_nhb.q(unit);
         for (long long i = tb; i < te; ++i, ++j) {
             if (j >= p.nst) {
                 const uint32_t par = ph ^ 1u;
@@ -460,16 +844,36 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                 }
             }
             const long long t0 = ti * T;
-            const long long seq_b = bk / p.n_kv_heads;
+            const long long seq_b = p.fd_hkv.q(bk);
             const long long kvh_p = bk - seq_b * p.n_kv_heads;
             long long len_b = p.seqlen;
             if (p.paged) {
                 const long long cl = p.ctx_lens[seq_b];
                 len_b = cl < 0 ? 0 : (cl > p.seqlen ? p.seqlen : cl);
             }
-            const int ntok = static_cast<int>(max(0LL, min(static_cast<long long>(T), len_b - t0)));
+            int ntok = static_cast<int>(max(0LL, min(static_cast<long long>(T), len_b - t0)));
             const long long rowbase = bk * p.kv_buf_len + t0;
             uint8_t* sb = smem + static_cast<size_t>(st) * p.stage_bytes;
+            if (p.paged) {
+                // Every page the tile touches must lie inside the cache; a tile
+                // with an out-of-range table entry copies nothing, records
+                // kDevBadBlock and is masked (the consumers read its live
+                // length from the stage).
+                bool bad = false;
+                if (ntok > 0) {
+                    const int* bt = p.block_tables + seq_b * p.max_blocks;
+                    const long long b0 = p.fd_bs.q(t0), b1 = p.fd_bs.q(t0 + ntok - 1);
+                    for (long long blk = b0 + lane; blk <= b1; blk += 32) {
+                        const long long page = bt[blk];
+                        bad |= page < 0 || page >= p.num_blocks;
+                    }
+                }
+                if (__any_sync(kFull, bad)) {
+                    ntok = 0;
+                    if (lane == 0) atomicExch(p.err, kDevBadBlock);
+                }
+                if (lane == 0) *reinterpret_cast<int*>(sb + p.off_ntok) = ntok;
+            }
             const int n8 = (ntok + 7) & ~7;
 
             // Scales that cannot use a bulk copy (unaligned slabs): plain loads.
@@ -487,13 +891,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                 const int* bt = p.block_tables + seq_b * p.max_blocks;
                 uint32_t bytes_k = new_unit ? HB * kHeadDim * 2 : 0, bytes_v = 0;
                 for (long long pos = t0; pos < t0 + ntok;) {
-                    const int off = static_cast<int>(pos % bs);
+                    const int off = static_cast<int>(p.fd_bs.r(pos));
                     const int n = static_cast<int>(min(static_cast<long long>(bs - off), t0 + ntok - pos));
                     const int nn8 = (n + 7) & ~7;
                     bytes_k += n * ROWB + (F::TOKK ? nn8 * 2 : 0);
                     bytes_v += n * ROWB + (F::TOKV ? nn8 * 2 : 0) + (F::ZV ? nn8 * 2 : 0);
                     if (F::KG && p.kg_smem)
-                        bytes_k += (F::ZK ? 2 : 1) * ((pos + n - 1) / p.group_size - pos / p.group_size + 1) *
+                        bytes_k += (F::ZK ? 2 : 1) * (p.fd_gs.q(pos + n - 1) - p.fd_gs.q(pos) + 1) *
                                    kHeadDim * 2;
                     pos += n;
                 }
@@ -504,12 +908,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                     const long long qo = (seq_b * p.n_heads + kvh_p * p.nhb * HB + hb * HB) * kHeadDim;
                     bulk_g2s(sb + p.off_q, p.q + qo, HB * kHeadDim * 2, &full[st], pol);
                 }
-                const long long g0 = F::KG ? t0 / p.group_size : 0;
+                const long long g0 = F::KG ? p.fd_gs.q(t0) : 0;
                 for (long long pos = t0; pos < t0 + ntok;) {
-                    const int off = static_cast<int>(pos % bs);
+                    const int off = static_cast<int>(p.fd_bs.r(pos));
                     const int n = static_cast<int>(min(static_cast<long long>(bs - off), t0 + ntok - pos));
                     const int nn8 = (n + 7) & ~7;
-                    const long long page = bt[pos / bs];
+                    const long long page = bt[p.fd_bs.q(pos)];
                     const long long row = (page * p.n_kv_heads + kvh_p) * bs + off;
                     const int d = static_cast<int>(pos - t0);
                     bulk_g2s(sb + d * ROWB, p.k + row * ROWB, n * ROWB, &full[st], pol);
@@ -518,9 +922,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                     if (F::TOKV) bulk_g2s(sb + p.off_vs + d * 2, p.vs + row, nn8 * 2, &fullv[st], pol);
                     if (F::ZV) bulk_g2s(sb + p.off_vz + d * 2, p.vz + row, nn8 * 2, &fullv[st], pol);
                     if (F::KG && p.kg_smem) {
-                        const long long ga = pos / p.group_size, gb2 = (pos + n - 1) / p.group_size;
-                        const long long gsrc = ((page * p.n_kv_heads + kvh_p) * (bs / p.group_size) +
-                                                off / p.group_size) * kHeadDim;
+                        const long long ga = p.fd_gs.q(pos), gb2 = p.fd_gs.q(pos + n - 1);
+                        const long long gsrc = ((page * p.n_kv_heads + kvh_p) * p.fd_gs.q(bs) +
+                                                p.fd_gs.q(off)) * kHeadDim;
                         const int gcnt = static_cast<int>(gb2 - ga + 1);
                         bulk_g2s(sb + p.off_kgs + (ga - g0) * kHeadDim * 2, p.ks + gsrc, gcnt * kHeadDim * 2,
                                  &full[st], pol);
@@ -539,8 +943,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                     bytes_v += (F::TOKV + F::ZV) * n8 * 2;
                 }
                 if (F::KG && p.kg_smem && ntok > 0) {
-                    g0 = static_cast<int>(t0) / p.group_size;
-                    const int g1 = (static_cast<int>(t0) + ntok - 1) / p.group_size;
+                    g0 = static_cast<int>(p.fd_gs.q(t0));
+                    const int g1 = static_cast<int>(p.fd_gs.q(t0 + ntok - 1));
                     ngrp = g1 - g0 + 1;
                     bytes_k += (F::ZK ? 2 : 1) * ngrp * kHeadDim * 2;
                 }
@@ -548,7 +952,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                 mbar_arrive_expect_tx(&full[st], bytes_k);
                 if (new_unit) {
                     const int hb = static_cast<int>(unit - bk * p.nhb);
-                    const long long b = bk / p.n_kv_heads;
+                    const long long b = p.fd_hkv.q(bk);
                     const long long kvh = bk - b * p.n_kv_heads;
                     const long long qo = (b * p.n_heads + kvh * p.nhb * HB + hb * HB) * kHeadDim;
                     bulk_g2s(sb + p.off_q, p.q + qo, HB * kHeadDim * 2, &full[st], pol);
@@ -577,15 +981,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
             if (++ti == p.tpu) {
                 ti = 0;
                 ++unit;
-                bk = unit / p.nhb;
+                bk = p.fd_nhb.q(unit);
             }
         }
         if (!ok) {
             // Let the copies already issued land before the CTA can exit.
             const long long first = j > p.nst ? j - p.nst : 0;
             for (long long jj = first; jj < j; ++jj) {
-                mbar_wait_bounded(&full[jj % p.nst], static_cast<uint32_t>((jj / p.nst) & 1));
-                mbar_wait_bounded(&fullv[jj % p.nst], static_cast<uint32_t>((jj / p.nst) & 1));
+                mbar_wait_bounded(&full[p.fd_nst.r(jj)], static_cast<uint32_t>(p.fd_nst.q(jj) & 1));
+                mbar_wait_bounded(&fullv[p.fd_nst.r(jj)], static_cast<uint32_t>(p.fd_nst.q(jj) & 1));
             }
             if (lane == 0) atomicExch(p.err, kDevWaitTimeout);
         }
@@ -604,8 +1008,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
     // either write the whole unit's output or publish this CTA's partial, take
     // the unit's ticket and, if this segment completes the unit, merge it.
     if (warp == kEpilogueWarp) {
-        constexpr int HBK = HB * kHeadDim;
-        const long long nhand = (te - 1) / p.tpu - tb / p.tpu;  // segment ends before the last
+        const long long nhand = p.fd_tpu.q(te - 1) - p.fd_tpu.q(tb);  // segment ends before the last
         for (long long k = 0; k < nhand; ++k) {
             if (!mbar_wait_bounded(epi_full, static_cast<uint32_t>(k & 1))) {
                 misc[0] = 1;
@@ -613,32 +1016,480 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                 break;
             }
             const EpiDesc d = *desc;
-            WarpCombine<HB> wc;
-            wc.load(mlb, lane);
-            if (d.whole) {
-                for (int o = lane; o < HBK; o += 32)
-                    p.out[d.qoff + o] = __float2half_rn(wc.combined(abuf, o) / pick<HB>(wc.L, o >> 7));
-                __syncwarp();
-                if (lane == 0) mbar_arrive(epi_empty);
-            } else {
-                float* sp = p.part + d.slot * SL;
-                for (int o = lane; o < HBK; o += 32) sp[o] = wc.combined(abuf, o);
-                if (lane < HB) {
-                    sp[HBK + lane] = pick<HB>(wc.M, lane);
-                    sp[HBK + HB + lane] = pick<HB>(wc.L, lane);
+            epilogue_handoff<HB>(p, d, mlb, abuf, epi_empty, lane);
+        }
+        return;
+    }
+
+    // ======================= scale warp (tensor-pipe INT4) =================
+    // For every tile, fold each K group's scales into q once for all consumer
+    // warps: W[group][head][lane block r][16 + 16 half2] in the QK B-fragment order
+    // (the rounded weights, then their rounding remainders),
+    // and the group's per-head constant (asym: sum_c q_c z_c; sym: -8 sum of
+    // the fed weights), written into the stage and released on wfull[stage].
+    if constexpr (MMA && F::KG) {
+        if (warp == kScaleWarp) {
+            // lane: block lr, k-step ks, half hf -> channels c_i = 32 lr + 8 ks +
+            // hf + 2 i (i = 0..3), byte i of B register [ks][hf] of every limb
+            constexpr int L = MmaFmt<FMT>::L;
+            constexpr float kFix = 8388607.f;  // 2^23 - 1: 24-bit signed fixed point
+            const int lr = lane >> 3, ks = (lane >> 1) & 3, hf = lane & 1;
+            const int cb = 32 * lr + 8 * ks;
+            float qv[HB][4];
+#pragma unroll
+            for (int h = 0; h < HB; ++h)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) qv[h][i] = 0.f;
+            int st = 0;
+            uint32_t ph = 0;
+            long long unit = p.fd_tpu.q(tb), ti = tb - unit * p.tpu, cur_unit = -1, bk = 0, seq_len = 0;
+            for (long long i = tb; i < te; ++i) {
+                if (misc[0] || !mbar_wait_bounded(&full[st], ph)) {
+                    misc[0] = 1;
+                    if (lane == 0) atomicExch(p.err, kDevWaitTimeout);
+                    break;
                 }
-                __syncwarp();  // the partial is written; the shared state is free again
-                if (lane == 0) mbar_arrive(epi_empty);
-                const UnitSpan span = unit_span(p, d.unit);
-                int last = 0;
-                if (lane == 0) last = unit_ticket(p, d.unit, span);
-                last = __shfl_sync(kFull, last, 0);
-                if (last) merge_segments<HB>(p, span, d.qoff, lane, 32);
+                const uint8_t* sb = smem + static_cast<size_t>(st) * p.stage_bytes;
+                if (unit != cur_unit) {
+                    cur_unit = unit;
+                    bk = p.fd_nhb.q(unit);
+                    const long long b = p.fd_hkv.q(bk);
+                    seq_len = p.seqlen;
+                    if (p.paged) {
+                        const long long cl = p.ctx_lens[b];
+                        seq_len = cl < 0 ? 0 : (cl > p.seqlen ? p.seqlen : cl);
+                    }
+                    const __half* sq = reinterpret_cast<const __half*>(sb + p.off_q);
+#pragma unroll
+                    for (int h = 0; h < HB; ++h) {
+                        const uint4 u = *reinterpret_cast<const uint4*>(sq + h * kHeadDim + cb);
+                        const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                        for (int i2 = 0; i2 < 4; ++i2) qv[h][i2] = half_of(uw[i2], hf) * p.qscale;
+                    }
+                }
+                const long long t0 = ti * T;
+                int ntok = static_cast<int>(max(0LL, min(static_cast<long long>(T), seq_len - t0)));
+                if (p.paged) ntok = *reinterpret_cast<const volatile int*>(sb + p.off_ntok);
+                if (ntok > 0) {
+                    const long long g0 = p.fd_gs.q(t0);
+                    const long long g1 = p.fd_gs.q(t0 + ntok - 1);
+                    uint32_t* bw = reinterpret_cast<uint32_t*>(smem + static_cast<size_t>(st) * p.stage_bytes + p.off_w);
+                    float* zk = reinterpret_cast<float*>(smem + static_cast<size_t>(st) * p.stage_bytes + p.off_zk);
+                    float* dq = zk + p.ngw * HB;
+#pragma unroll 1
+                    for (long long ga = g0; ga <= g1; ++ga) {
+                        const int gi = static_cast<int>(ga - g0);
+                        const __half* gsp;
+                        const __half* gzp = nullptr;
+                        if (p.kg_smem) {
+                            gsp = reinterpret_cast<const __half*>(sb + p.off_kgs) + gi * kHeadDim;
+                            if (F::ZK) gzp = reinterpret_cast<const __half*>(sb + p.off_kgz) + gi * kHeadDim;
+                        } else {
+                            long long gb = (bk * p.ng_buf + ga) * kHeadDim;
+                            if (p.paged) {
+                                const long long pos = ga * p.group_size;
+                                const long long sq2 = p.fd_hkv.q(bk);
+                                const long long page =
+                                    checked_page(p, p.block_tables[sq2 * p.max_blocks + p.fd_bs.q(pos)]);
+                                gb = ((page * p.n_kv_heads + (bk - sq2 * p.n_kv_heads)) * p.fd_gs.q(p.block_size) +
+                                      p.fd_gs.q(p.fd_bs.r(pos))) * kHeadDim;
+                            }
+                            gsp = p.ks + gb;
+                            if (F::ZK) gzp = p.kz + gb;
+                        }
+                        float sv[4], zv4[4];
+                        {
+                            const uint4 u = *reinterpret_cast<const uint4*>(gsp + cb);
+                            const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                            for (int i2 = 0; i2 < 4; ++i2) sv[i2] = half_of(uw[i2], hf);
+                            if (F::ZK) {
+                                const uint4 uz = *reinterpret_cast<const uint4*>(gzp + cb);
+                                const uint32_t zw[4] = {uz.x, uz.y, uz.z, uz.w};
+#pragma unroll
+                                for (int i2 = 0; i2 < 4; ++i2) zv4[i2] = half_of(zw[i2], hf);
+                            }
+                        }
+                        // per-head maximum |w| sets the fixed-point step
+                        float w[HB][4], mx[HB];
+#pragma unroll
+                        for (int h = 0; h < HB; ++h) {
+                            mx[h] = 0.f;
+#pragma unroll
+                            for (int i2 = 0; i2 < 4; ++i2) {
+                                w[h][i2] = qv[h][i2] * sv[i2];
+                                mx[h] = fmaxf(mx[h], fabsf(w[h][i2]));
+                            }
+                        }
+                        int mh;
+                        const float mres = lane_reduce_scatter<HB>(mx, lane, mh, OpMax{});
+                        float zp[HB];
+                        int ip[HB];
+#pragma unroll
+                        for (int h = 0; h < HB; ++h) {
+                            const float amax = __shfl_sync(kFull, mres, lane_of_result<HB>(h));
+                            const float inv = amax > 0.f ? kFix / amax : 0.f;
+                            int wi[4];
+#pragma unroll
+                            for (int i2 = 0; i2 < 4; ++i2)  // clamp: w * inv can round up to 2^23 at the maximum
+                                wi[i2] = max(-8388607, min(8388607, __float2int_rn(w[h][i2] * inv)));
+                            uint32_t* dst = bw + ((gi * HB + h) * 4 + lr) * (L * 8) + 2 * ks + hf;
+#pragma unroll
+                            for (int l = 0; l < L; ++l) dst[8 * l] = pack_bytes(wi[0], wi[1], wi[2], wi[3], 8 * (L - 1 - l));
+                            if (F::ZK) {
+                                zp[h] = fmaf(qv[h][0], zv4[0], fmaf(qv[h][1], zv4[1], fmaf(qv[h][2], zv4[2], qv[h][3] * zv4[3])));
+                            } else {
+                                ip[h] = (wi[0] + wi[1]) + (wi[2] + wi[3]);
+                            }
+                            if (lane == 0) dq[gi * HB + h] = amax > 0.f ? amax / kFix : 0.f;
+                        }
+                        int zh;
+                        if (F::ZK) {
+                            const float zs = lane_reduce_scatter<HB>(zp, lane, zh, OpSum{});
+                            if ((lane & (32 / HB - 1)) == 0) zk[gi * HB + zh] = zs;
+                        } else {
+                            // sym: codes enter as c + 8; -8 * (step * sum of the fixed-point weights)
+                            const int zs = lane_reduce_scatter<HB>(ip, lane, zh, OpSum{});
+                            if ((lane & (32 / HB - 1)) == 0)
+                                zk[gi * HB + zh] = -8.f * (mres > 0.f ? mres / kFix : 0.f) * static_cast<float>(zs);
+                        }
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&wfull[st]);
+                if (++st == p.nst) {
+                    st = 0;
+                    ph ^= 1u;
+                }
+                if (++ti == p.tpu) {
+                    ti = 0;
+                    ++unit;
+                }
+            }
+            return;
+        }
+    }
+
+    // ======================= consumer warps (tensor pipe) =================
+    // A compact rolled loop over the warp's 16-position m-tiles (TW / 16 per
+    // tile), software-pipelined by one m-tile: iteration k issues the QK MMAs
+    // of m-tile k, then finishes m-tile k - 1 (scores, softmax, PV), so the QK
+    // chain of one m-tile overlaps the softmax and PV of the previous one.
+    if constexpr (MMA) {
+        using M = MmaFmt<FMT>;
+        const int w = warp;
+        const int g = lane >> 2, r = lane & 3;
+        const int rg = rho(g);
+        const int vr = rho(2 * r);
+        constexpr int MT = TW / 16;         // m-tiles per warp per tile
+        constexpr float kSub = 16777216.f;  // 2^24: subnormal code units
+        constexpr float kScHi = M::I4 ? kSub / 16.f : kSub;  // INT4 c_hi rows were fed as 16 n
+        const int wt0 = w * TW;
+        const long long first_unit_of_cta = p.fd_tpu.q(tb);
+        long long nhand = 0;
+        UnitSpan* last_span = reinterpret_cast<UnitSpan*>(smem + p.off_misc + 16 + sizeof(EpiDesc));
+        if (tid == 0) *last_span = unit_span(p, p.fd_tpu.q(te - 1));
+
+        float acc[8][4];
+        float m_run[2], l_run[2], zv[2], lf[2];
+        constexpr int L = M::L;
+        uint32_t Bq[L][4][2];  // fixed-point limbs of the folded QK weights (B fragments)
+        float zk[2], dk[2];    // per-head score constant and fixed-point step of the weights loaded
+        bool aborted = false;
+        auto reset_state = [&]() {
+#pragma unroll
+            for (int mt = 0; mt < 8; ++mt)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) acc[mt][c] = 0.f;
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) m_run[hh] = -INFINITY, l_run[hh] = 0.f, zv[hh] = 0.f, lf[hh] = 0.f;
+        };
+        reset_state();
+#pragma unroll
+        for (int l = 0; l < L; ++l)
+#pragma unroll
+            for (int k2 = 0; k2 < 4; ++k2) Bq[l][k2][0] = Bq[l][k2][1] = 0u;
+        zk[0] = zk[1] = dk[0] = dk[1] = 0.f;
+        auto fail = [&]() {
+            aborted = true;
+            misc[0] = 1;
+            if (lane == 0) atomicExch(p.err, kDevWaitTimeout);
+        };
+
+        // issue cursor (m-tile whose QK is issued next) and process cursor
+        int ist = 0, imi = 0, pst = 0, pmi = 0;
+        uint32_t iph = 0, pph = 0;
+        long long iunit = p.fd_tpu.q(tb), iti = tb - iunit * p.tpu, loaded_unit = -1, iseq = 0;
+        long long punit = iunit, pti = iti;
+        int invl = 0, igi = -1;  // warp's valid positions in the issue tile; K group loaded
+        int dn[L][4];            // the issued m-tile's raw QK accumulators (one per limb)
+        float zn[2], dqn[2];     // and its per-head constants / fixed-point steps
+        int nrow = 0;            // its valid rows (0..16)
+        const long long nm = (te - tb) * MT;
+
+        for (long long k = 0; k <= nm; ++k) {
+            int dc[L][4];
+            float zc[2], dqc[2];
+#pragma unroll
+            for (int l = 0; l < L; ++l)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) dc[l][c] = dn[l][c];
+            zc[0] = zn[0], zc[1] = zn[1];
+            dqc[0] = dqn[0], dqc[1] = dqn[1];
+            const int crow = nrow;
+
+            // ------------- issue the QK of m-tile k -------------
+            if (k < nm) {
+                const uint8_t* sb = smem + static_cast<size_t>(ist) * p.stage_bytes;
+                if (imi == 0) {
+                    if (iunit != loaded_unit) {
+                        loaded_unit = iunit;
+                        iseq = p.seqlen;
+                        if (p.paged) {
+                            const long long cl = p.ctx_lens[p.fd_hkv.q(p.fd_nhb.q(iunit))];
+                            iseq = cl < 0 ? 0 : (cl > p.seqlen ? p.seqlen : cl);
+                        }
+                        if constexpr (FMT == kI8) {
+                            if (!aborted && (misc[0] || !mbar_wait_bounded(&full[ist], iph))) fail();
+                            // q * softmax_scale * log2 e for head g over the lane block's
+                            // 32 channels as 16-bit fixed point (two limbs); the step is
+                            // the head's max |w| / 32767
+                            const __half* qp = reinterpret_cast<const __half*>(sb + p.off_q) +
+                                               (g < HB ? g : 0) * kHeadDim + 32 * r;
+                            float wv[32];
+                            float mxw = 0.f;
+#pragma unroll
+                            for (int c4 = 0; c4 < 4; ++c4) {
+                                const uint4 u = *reinterpret_cast<const uint4*>(qp + 8 * c4);
+                                const __half* hv = reinterpret_cast<const __half*>(&u);
+#pragma unroll
+                                for (int i2 = 0; i2 < 8; ++i2) {
+                                    wv[8 * c4 + i2] = g < HB ? __half2float(hv[i2]) * p.qscale : 0.f;
+                                    mxw = fmaxf(mxw, fabsf(wv[8 * c4 + i2]));
+                                }
+                            }
+                            mxw = fmaxf(mxw, __shfl_xor_sync(kFull, mxw, 1));
+                            mxw = fmaxf(mxw, __shfl_xor_sync(kFull, mxw, 2));
+                            const float inv = mxw > 0.f ? 32767.f / mxw : 0.f;
+#pragma unroll
+                            for (int k2 = 0; k2 < 4; ++k2)
+#pragma unroll
+                                for (int hf = 0; hf < 2; ++hf) {
+                                    const int c0 = 8 * k2 + 4 * hf;
+                                    auto fx = [&](float x) { return max(-32767, min(32767, __float2int_rn(x * inv))); };
+                                    const int i0 = fx(wv[c0]), i1 = fx(wv[c0 + 1]), i2 = fx(wv[c0 + 2]), i3 = fx(wv[c0 + 3]);
+                                    Bq[0][k2][hf] = pack_bytes(i0, i1, i2, i3, 8);
+                                    Bq[1][k2][hf] = pack_bytes(i0, i1, i2, i3, 0);
+                                }
+                            const float step = mxw > 0.f ? mxw / 32767.f : 0.f;
+                            dk[0] = __shfl_sync(kFull, step, 8 * r);
+                            dk[1] = __shfl_sync(kFull, step, 8 * r + 4);
+                        }
+                    }
+                    if (!aborted && (misc[0] || !mbar_wait_bounded(&full[ist], iph) ||
+                                     (F::KG && !mbar_wait_bounded(&wfull[ist], iph))))
+                        fail();
+                    int ntok = static_cast<int>(max(0LL, min(static_cast<long long>(T), iseq - iti * T)));
+                    if (p.paged) ntok = *reinterpret_cast<const volatile int*>(sb + p.off_ntok);
+                    invl = ntok - wt0;
+                    igi = -1;
+                }
+                nrow = aborted ? 0 : max(0, min(16, invl - 16 * imi));
+                if (nrow > 0) {
+                    if constexpr (F::KG) {
+                        const long long t0 = iti * T;
+                        const int gi = static_cast<int>(p.fd_gs.q(t0 + wt0 + 16 * imi) - p.fd_gs.q(t0));
+                        if (gi != igi) {
+                            igi = gi;
+                            const uint4* bw = reinterpret_cast<const uint4*>(
+                                sb + p.off_w + ((gi * HB + (g < HB ? g : 0)) * 4 + r) * (L * 32));
+#pragma unroll
+                            for (int l = 0; l < L; ++l) {
+                                const uint4 u0 = bw[2 * l], u1 = bw[2 * l + 1];
+                                Bq[l][0][0] = u0.x, Bq[l][0][1] = u0.y, Bq[l][1][0] = u0.z, Bq[l][1][1] = u0.w;
+                                Bq[l][2][0] = u1.x, Bq[l][2][1] = u1.y, Bq[l][3][0] = u1.z, Bq[l][3][1] = u1.w;
+                            }
+                            if (g >= HB) {
+#pragma unroll
+                                for (int l = 0; l < L; ++l)
+#pragma unroll
+                                    for (int k2 = 0; k2 < 4; ++k2) Bq[l][k2][0] = Bq[l][k2][1] = 0u;
+                            }
+                            const float* zkp = reinterpret_cast<const float*>(sb + p.off_zk) + gi * HB;
+                            const float* dqp = zkp + p.ngw * HB;
+                            zk[0] = 2 * r < HB ? zkp[2 * r] : 0.f;
+                            zk[1] = 2 * r + 1 < HB ? zkp[2 * r + 1] : 0.f;
+                            dk[0] = 2 * r < HB ? dqp[2 * r] : 0.f;
+                            dk[1] = 2 * r + 1 < HB ? dqp[2 * r + 1] : 0.f;
+                        }
+                    }
+                    qk_mtile_int<FMT, L>(sb + (wt0 + 16 * imi + rg) * ROWB + (M::I4 ? 16 : 32) * r, Bq, dn);
+                    zn[0] = zk[0], zn[1] = zk[1];
+                    dqn[0] = dk[0], dqn[1] = dk[1];
+                }
+                if (++imi == MT) {
+                    imi = 0;
+                    if (++ist == p.nst) {
+                        ist = 0;
+                        iph ^= 1u;
+                    }
+                    if (++iti == p.tpu) {
+                        iti = 0;
+                        ++iunit;
+                    }
+                }
+            }
+            if (k == 0) continue;
+
+            // ------------- finish m-tile k - 1: scores, softmax, PV -------------
+            const uint8_t* sb = smem + static_cast<size_t>(pst) * p.stage_bytes;
+            if (pmi == 0 && !aborted && (misc[0] || !mbar_wait_bounded(&fullv[pst], pph))) fail();
+            if (!aborted && crow > 0) {
+                const int row = wt0 + 16 * pmi + rg;
+                const bool ok0 = rg < crow, ok1 = rg + 8 < crow;  // rows past the live length: masked
+                // raw dot products from the integer limbs (exact in fp32)
+                float dv[4];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    if constexpr (L == 2)
+                        dv[c] = static_cast<float>(dc[0][c] * 256 + dc[1][c]);
+                    else
+                        dv[c] = fmaf(static_cast<float>(dc[0][c] * 256 + dc[1][c]), 256.f, static_cast<float>(dc[2][c]));
+                }
+                float sc[4];
+                if constexpr (FMT == kI8) {
+                    const __half* sks = reinterpret_cast<const __half*>(sb + p.off_ks);
+                    const float k0 = __half2float(sks[row]), k1 = __half2float(sks[row + 8]);
+                    sc[0] = dv[0] * dqc[0] * k0;
+                    sc[1] = dv[1] * dqc[1] * k0;
+                    sc[2] = dv[2] * dqc[0] * k1;
+                    sc[3] = dv[3] * dqc[1] * k1;
+                } else {
+                    sc[0] = fmaf(dv[0], dqc[0], zc[0]);
+                    sc[1] = fmaf(dv[1], dqc[1], zc[1]);
+                    sc[2] = fmaf(dv[2], dqc[0], zc[0]);
+                    sc[3] = fmaf(dv[3], dqc[1], zc[1]);
+                }
+                if (!ok0) sc[0] = sc[1] = -INFINITY;
+                if (!ok1) sc[2] = sc[3] = -INFINITY;
+                // Online softmax (log2 domain). The running maximum is only
+                // raised when a score exceeds it by more than kTau (weights up
+                // to 2^kTau, which keeps p * v_scale inside fp16 for every fp16
+                // V); the common case costs one vote.
+                float mx0 = fmaxf(sc[0], sc[2]), mx1 = fmaxf(sc[1], sc[3]);
+                if (__any_sync(kFull, mx0 > m_run[0] + M::kTau || mx1 > m_run[1] + M::kTau)) {
+                    mx0 = fmaxf(mx0, __shfl_xor_sync(kFull, mx0, 4));
+                    mx1 = fmaxf(mx1, __shfl_xor_sync(kFull, mx1, 4));
+                    mx0 = fmaxf(mx0, __shfl_xor_sync(kFull, mx0, 8));
+                    mx1 = fmaxf(mx1, __shfl_xor_sync(kFull, mx1, 8));
+                    mx0 = fmaxf(mx0, __shfl_xor_sync(kFull, mx0, 16));
+                    mx1 = fmaxf(mx1, __shfl_xor_sync(kFull, mx1, 16));
+                    const float mn0 = fmaxf(m_run[0], mx0), mn1 = fmaxf(m_run[1], mx1);
+                    const float a0 = mn0 == -INFINITY ? 1.f : fast_exp2(m_run[0] - mn0);
+                    const float a1 = mn1 == -INFINITY ? 1.f : fast_exp2(m_run[1] - mn1);
+                    m_run[0] = mn0;
+                    m_run[1] = mn1;
+                    l_run[0] *= a0, zv[0] *= a0, lf[0] *= a0;
+                    l_run[1] *= a1, zv[1] *= a1, lf[1] *= a1;
+#pragma unroll
+                    for (int mt = 0; mt < 8; ++mt) {
+                        acc[mt][0] *= a0;
+                        acc[mt][1] *= a1;
+                        acc[mt][2] *= a0;
+                        acc[mt][3] *= a1;
+                    }
+                }
+                const float mu0 = m_run[0] == -INFINITY ? 0.f : m_run[0];
+                const float mu1 = m_run[1] == -INFINITY ? 0.f : m_run[1];
+                const float p0 = fast_exp2(sc[0] - mu0), p1 = fast_exp2(sc[1] - mu1);
+                const float p2 = fast_exp2(sc[2] - mu0), p3 = fast_exp2(sc[3] - mu1);
+                l_run[0] += p0 + p2;
+                l_run[1] += p1 + p3;
+                const __half* svs = reinterpret_cast<const __half*>(sb + p.off_vs);
+                const float v0 = ok0 ? __half2float(svs[row]) : 0.f;
+                const float v1 = ok1 ? __half2float(svs[row + 8]) : 0.f;
+                if (F::ZV) {
+                    const __half* svz = reinterpret_cast<const __half*>(sb + p.off_vz);
+                    const float z0 = ok0 ? __half2float(svz[row]) : 0.f;
+                    const float z1 = ok1 ? __half2float(svz[row + 8]) : 0.f;
+                    zv[0] = fmaf(p0, z0, fmaf(p2, z1, zv[0]));
+                    zv[1] = fmaf(p1, z0, fmaf(p3, z1, zv[1]));
+                }
+                const uint32_t pr0 = pack_h2(p0 * v0, p1 * v0);
+                const uint32_t pr1 = pack_h2(p2 * v1, p3 * v1);
+                if (!F::ZV) {
+                    // the exact sum of the fed weights cancels the V code offset
+                    fma_h2_2acc(pr0, 0x3c003c00u, lf[0], lf[1]);
+                    fma_h2_2acc(pr1, 0x3c003c00u, lf[0], lf[1]);
+                }
+                pv_kstep<FMT>(sb + p.off_v + (wt0 + 16 * pmi + vr) * ROWB + (M::I4 ? 8 : 16) * g,
+                              movmatrix_trans(pr0), movmatrix_trans(pr1), acc);
+            }
+            if (++pmi < MT) continue;
+
+            // ------------- the tile is finished -------------
+            pmi = 0;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[pst]);
+            const long long i = tb + (k - 1) / MT;
+            if (pti == p.tpu - 1 || i == te - 1) {
+                // end of a unit segment
+                const bool final_seg = (i == te - 1);
+                const bool whole = (pti == p.tpu - 1) && (punit * p.tpu >= tb);
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+                    for (int m = 4; m < 32; m <<= 1) {
+                        l_run[hh] += __shfl_xor_sync(kFull, l_run[hh], m);
+                        zv[hh] += __shfl_xor_sync(kFull, zv[hh], m);
+                        lf[hh] += __shfl_xor_sync(kFull, lf[hh], m);
+                    }
+                wait_handoff_free(p, epi_empty, misc, nhand, lane);
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) {
+                    const int h = 2 * r + hh;
+                    if (h < HB) {
+                        if (g == 0) {
+                            mlb[(w * HB + h) * 3] = m_run[hh];
+                            mlb[(w * HB + h) * 3 + 1] = l_run[hh];
+                        }
+                        const float add = F::ZV ? zv[hh] : -M::VOFF * lf[hh];
+                        float o[16];
+#pragma unroll
+                        for (int mt = 0; mt < 8; ++mt) {
+                            o[2 * mt] = fmaf(acc[mt][hh], kSub, add);
+                            o[2 * mt + 1] = fmaf(acc[mt][2 + hh], kScHi, add);
+                        }
+                        float4* dst = reinterpret_cast<float4*>(abuf + (w * HB + h) * kHeadDim + 16 * g);
+#pragma unroll
+                        for (int q4 = 0; q4 < 4; ++q4)
+                            dst[q4] = make_float4(o[4 * q4], o[4 * q4 + 1], o[4 * q4 + 2], o[4 * q4 + 3]);
+                    }
+                }
+                reset_state();
+                const long long bk = p.fd_nhb.q(punit);
+                const long long hb = punit - bk * p.nhb;
+                const long long b = p.fd_hkv.q(bk);
+                const long long kvh = bk - b * p.n_kv_heads;
+                const long long qoff = (b * p.n_heads + kvh * p.nhb * HB + hb * HB) * kHeadDim;
+                finish_segment<HB>(p, final_seg, whole, punit, qoff,
+                                   2 * cta + (punit == first_unit_of_cta ? 0 : 1), nhand, desc, epi_full, misc,
+                                   mlb, abuf, last_span, w, lane, tid);
+            }
+            if (++pst == p.nst) {
+                pst = 0;
+                pph ^= 1u;
+            }
+            if (++pti == p.tpu) {
+                pti = 0;
+                ++punit;
             }
         }
         return;
     }
 
+    if constexpr (!MMA) {
     // ======================= consumer warps ===============================
     const int w = warp;
     const int grp = lane >> 3;
@@ -655,16 +1506,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
     const int qpl = head_of_lane<QG>(lane & 7);            // pass within the group
     const int hh = head_of_lane<HB>((lane & 7) >> LQG);     // head
     const bool prim = ((lane & 7) >> LQV) == 0;            // not a duplicate
-    const int nct = kNCW * 32;
 
     uint16_t* pbuf = reinterpret_cast<uint16_t*>(smem + p.off_work) + w * TW * HB;  // p as f16
-    const long long first_unit_of_cta = tb / p.tpu;
+    const long long first_unit_of_cta = p.fd_tpu.q(tb);
     long long nhand = 0;  // segments handed to the epilogue warp so far
     // span of the CTA's last unit, needed right after its final segment;
     // computed now, while the first tiles are still in flight, and kept in
     // shared memory (read after the final segment's barriers)
     UnitSpan* last_span = reinterpret_cast<UnitSpan*>(smem + p.off_misc + 16 + sizeof(EpiDesc));
-    if (tid == 0) *last_span = unit_span(p, (te - 1) / p.tpu);
+    if (tid == 0) *last_span = unit_span(p, p.fd_tpu.q(te - 1));
 
     float m_run = -INFINITY, l_run = 0.f;
     float acc[HB][PVC];
@@ -686,7 +1536,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
 
     int st = 0;
     uint32_t ph = 0;
-    long long unit = tb / p.tpu;
+    long long unit = p.fd_tpu.q(tb);
     long long ti = tb - unit * p.tpu;
     for (long long i = tb; i < te; ++i) {
         const bool new_unit = (unit != cur_unit);
@@ -695,9 +1545,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
             cur_unit = unit;
             seg_t0 = ti;
             cur_g = -1;
-            bk = unit / p.nhb;
+            bk = p.fd_nhb.q(unit);
             const int hb = static_cast<int>(unit - bk * p.nhb);
-            const long long b = bk / p.n_kv_heads;
+            const long long b = p.fd_hkv.q(bk);
             const int kvh = static_cast<int>(bk - b * p.n_kv_heads);
             qoff = (b * p.n_heads + static_cast<long long>(kvh) * p.nhb * HB + hb * HB) * kHeadDim;
             seq_len = p.seqlen;
@@ -720,7 +1570,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                 if (lane == 0) atomicExch(p.err, kDevWaitTimeout);
             }
         }
-        LIK_TL(tid == 0 && new_unit && i != tb, 11);
         if (new_unit) {
             // q for the HB heads arrived with this stage (the producer copies it
             // into the first stage of every unit segment)
@@ -765,10 +1614,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                 }
             }
         }
-        LIK_TL(tid == 0 && i == tb, 1);
 
         const long long t0 = ti * T;
-        const int ntok = static_cast<int>(max(0LL, min(static_cast<long long>(T), seq_len - t0)));
+        int ntok = static_cast<int>(max(0LL, min(static_cast<long long>(T), seq_len - t0)));
+                if (p.paged) ntok = *reinterpret_cast<const volatile int*>(smem + static_cast<size_t>(st) * p.stage_bytes + p.off_ntok);
         const uint8_t* sb = smem + static_cast<size_t>(st) * p.stage_bytes;
         const int wt0 = w * TW;
 
@@ -793,17 +1642,17 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                 const __half* gsp;
                 const __half* gzp = nullptr;
                 if (p.kg_smem) {
-                    const int g0 = static_cast<int>(t0) / p.group_size;
+                    const int g0 = static_cast<int>(p.fd_gs.q(t0));
                     gsp = reinterpret_cast<const __half*>(sb + p.off_kgs) + (g - g0) * kHeadDim;
                     if (F::ZK) gzp = reinterpret_cast<const __half*>(sb + p.off_kgz) + (g - g0) * kHeadDim;
                 } else {
                     long long gb = (bk * p.ng_buf + g) * kHeadDim;
                     if (p.paged) {
                         const long long pos = static_cast<long long>(g) * p.group_size;
-                        const long long sq = bk / p.n_kv_heads;
-                        const long long page = p.block_tables[sq * p.max_blocks + pos / p.block_size];
+                        const long long sq = p.fd_hkv.q(bk);
+                        const long long page = checked_page(p, p.block_tables[sq * p.max_blocks + p.fd_bs.q(pos)]);
                         gb = ((page * p.n_kv_heads + (bk - sq * p.n_kv_heads)) *
-                                  (p.block_size / p.group_size) + (pos % p.block_size) / p.group_size) *
+                                  p.fd_gs.q(p.block_size) + p.fd_gs.q(p.fd_bs.r(pos))) *
                              kHeadDim;
                     }
                     gsp = p.ks + gb;
@@ -836,8 +1685,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
             bool group_checks = false;
             if constexpr (F::KG) {
                 const int pos_lo = static_cast<int>(t0) + wt0;
-                const int g_lo = pos_lo / p.group_size;
-                if (g_lo == (pos_lo + nval - 1) / p.group_size) {
+                const int g_lo = static_cast<int>(p.fd_gs.q(pos_lo));
+                if (g_lo == static_cast<int>(p.fd_gs.q(pos_lo + nval - 1))) {
                     if (g_lo != cur_g) load_group(g_lo);
                 } else {
                     group_checks = true;
@@ -879,7 +1728,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
                             i8x4_to_h2_offset(ka.w, kk[6], kk[7]);
                         } else {
                             const int tabs = static_cast<int>(t0) + tt;
-                            if (CHECK && (cur_g < 0 || tabs >= gnext)) load_group(tabs / p.group_size);
+                            if (CHECK && (cur_g < 0 || tabs >= gnext)) load_group(static_cast<int>(p.fd_gs.q(tabs)));
                             const uint2 kw = *reinterpret_cast<const uint2*>(row + jl * 8);
                             half2 c0[4], c1[4];
                             i4x8_to_h2<F::SIGNED>(kw.x, c0);
@@ -1047,20 +1896,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
         if (ti == p.tpu - 1 || i == te - 1) {
             const bool final_seg = (i == te - 1);
             const bool whole = (seg_t0 == 0 && ti == p.tpu - 1);
-            LIK_TL(tid == 0 && final_seg, 4);
             if (PVC == 8) {
 #pragma unroll
                 for (int h = 0; h < HB; ++h)
 #pragma unroll
                     for (int c = 0; c < 8; ++c) acc[h][c] += __shfl_xor_sync(kFull, acc[h][c], 16);
             }
-            // the epilogue warp has read the previous hand-off
-            if (lane == 0 && nhand > 0 &&
-                !mbar_wait_bounded(epi_empty, static_cast<uint32_t>((nhand - 1) & 1))) {
-                misc[0] = 1;
-                atomicExch(p.err, kDevWaitTimeout);
-            }
-            __syncwarp();
+            wait_handoff_free(p, epi_empty, misc, nhand, lane);
             if (grp == 0 && prim && qpl == 0) {
                 mlb[(w * HB + hh) * 3] = m_run;
                 mlb[(w * HB + hh) * 3 + 1] = l_run;
@@ -1086,42 +1928,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
             for (int h = 0; h < HB; ++h)
 #pragma unroll
                 for (int c = 0; c < PVC; ++c) acc[h][c] = 0.f;
-            if (!final_seg) {
-                if (w == 0 && lane == 0) {
-                    EpiDesc d;
-                    d.unit = unit;
-                    d.qoff = qoff;
-                    d.slot = 2 * cta + (unit == first_unit_of_cta ? 0 : 1);
-                    d.whole = whole ? 1 : 0;
-                    d.pad = 0;
-                    *desc = d;
-                }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(epi_full);  // release: the state and descriptor
-                ++nhand;
-            } else {
-                named_bar_sync(1, nct);  // every warp's state is in shared memory
-                LIK_TL(tid == 0, 5);
-                WarpCombine<HB> wc;
-                wc.load(mlb, lane);
-                if (whole) {
-                    for (int o = tid; o < HB * kHeadDim; o += nct)
-                        p.out[qoff + o] = __float2half_rn(wc.combined(abuf, o) / pick<HB>(wc.L, o >> 7));
-                } else {
-                    const long long slot = 2 * cta + (unit == first_unit_of_cta ? 0 : 1);
-                    float* sp = p.part + slot * SL;
-                    for (int o = tid; o < HB * kHeadDim; o += nct) sp[o] = wc.combined(abuf, o);
-                    if (tid < HB) {
-                        sp[HB * kHeadDim + tid] = pick<HB>(wc.M, tid);
-                        sp[HB * kHeadDim + HB + tid] = pick<HB>(wc.L, tid);
-                    }
-                    named_bar_sync(1, nct);  // the whole partial is written
-                    if (tid == 0) misc[1] = unit_ticket(p, unit, *last_span) ? 1 : 0;
-                    named_bar_sync(1, nct);
-                    LIK_TL(tid == 0, 6);
-                    if (misc[1]) merge_segments<HB>(p, *last_span, qoff, tid, nct);
-                }
-            }
+            finish_segment<HB>(p, final_seg, whole, unit, qoff, 2 * cta + (unit == first_unit_of_cta ? 0 : 1), nhand,
+                               desc, epi_full, misc, mlb, abuf, last_span, w, lane, tid);
         }
         if (++st == p.nst) {
             st = 0;
@@ -1131,18 +1939,24 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
             ti = 0;
             ++unit;
         }
-        LIK_TL(tid == 0 && i == te - 2, 2);
     }
-    LIK_TL(tid == 0, 3);
+    }  // !MMA
 }
 
 // ---- host side ------------------------------------------------------------
 
-int heads_per_unit(int64_t group, int fmt) {
-    // Eight heads per unit need more registers than the INT8/INT4 paths have
-    // (168 per thread at 10 warps per SM); those formats split a group of 8
-    // into two units of 4.
-    if (group % 8 == 0 && fmt == kF16) return 8;
+// INT8 and INT4 run QK / PV on the tensor pipe when no K group straddles a
+// 16-position MMA tile (INT4 group sizes that are multiples of 16); other INT4
+// group sizes and fp16 use the CUDA-core consumer.
+bool decode_uses_mma(int fmt, int64_t group_size) {
+    return fmt == kI8 || ((fmt == kI4Sym || fmt == kI4Asym) && group_size > 0 && group_size % 16 == 0);
+}
+
+int heads_per_unit(int64_t group, int fmt, bool mma) {
+    // The tensor-pipe consumer covers eight heads per MMA column block; the
+    // CUDA-core INT8/INT4 consumer has registers for four (168 per thread at
+    // 10 warps per SM) and splits a group of 8 into two units.
+    if (group % 8 == 0 && (fmt == kF16 || mma)) return 8;
     if (group % 4 == 0) return 4;
     if (group % 2 == 0) return 2;
     return 1;
@@ -1157,6 +1971,8 @@ static size_t partial_region_bytes(int sm_count) {
     return align_up(static_cast<size_t>(2) * sm_count * (8 * kHeadDim + 2 * 8) * 4, 256);
 }
 
+size_t decode_counter_offset(int sm_count) { return kWsErrBytes + partial_region_bytes(sm_count); }
+
 size_t decode_workspace_bytes(int64_t batch, int64_t n_heads, int64_t n_kv_heads, int sm_count) {
     if (batch <= 0 || n_kv_heads <= 0 || n_heads <= 0) return kWsErrBytes;
     const int64_t n_units = batch * n_heads;  // upper bound over every heads-per-unit choice
@@ -1165,7 +1981,7 @@ size_t decode_workspace_bytes(int64_t batch, int64_t n_heads, int64_t n_kv_heads
 
 namespace {
 
-template <int FMT, int HB>
+template <int FMT, int HB, bool MMA>
 lik_status launch_t(const DecodeArgs& a, const DeviceInfo& di, cudaStream_t stream, std::string& err) {
     using F = Fmt<FMT>;
     constexpr int T = F::T;
@@ -1194,7 +2010,18 @@ lik_status launch_t(const DecodeArgs& a, const DeviceInfo& di, cudaStream_t stre
     p.ctx_lens = a.context_lens;
     p.block_size = static_cast<int>(a.block_size);
     p.max_blocks = static_cast<int>(a.max_blocks);
+    p.num_blocks = a.num_blocks;
     p.qscale = a.softmax_scale * kLog2e;
+    // 32-bit index arithmetic in the kernel (launch-constant divisors)
+    if (p.total_tiles >= (int64_t{1} << 31) || a.batch * a.n_kv_heads >= (int64_t{1} << 31)) {
+        err = "too many work tiles for one launch (batch * n_heads * seqlen / tile above 2^31)";
+        return LIK_ERR_UNSUPPORTED;
+    }
+    p.fd_tpu = make_fdiv(static_cast<uint32_t>(p.tpu));
+    p.fd_nhb = make_fdiv(static_cast<uint32_t>(p.nhb));
+    p.fd_hkv = make_fdiv(static_cast<uint32_t>(p.n_kv_heads));
+    p.fd_gs = make_fdiv(static_cast<uint32_t>(p.group_size));
+    p.fd_bs = make_fdiv(static_cast<uint32_t>(p.block_size > 0 ? p.block_size : 1));
 
     // Per-token scales ride the bulk copy when every tile's scale run is
     // 16-byte aligned and a multiple of 16 bytes (rounded up to 8 tokens,
@@ -1229,17 +2056,30 @@ lik_status launch_t(const DecodeArgs& a, const DeviceInfo& di, cudaStream_t stre
     off = static_cast<int>(align_up(off, 16));
     p.off_q = off;
     off += HB * kHeadDim * 2;
+    p.off_ntok = off;  // paged: the tile's live length (0 when masked)
+    off += 16;
+    if (MMA && F::KG) {
+        // fixed-point limbs of the folded K weights, per-head score constants
+        // and fixed-point steps of the tile's K groups
+        p.ngw = static_cast<int>(std::min<int64_t>(a.n_groups_buf, (T + a.group_size - 1) / a.group_size + 1));
+        off = static_cast<int>(align_up(off, 16));
+        p.off_w = off;
+        off += p.ngw * HB * 4 * MmaFmt<FMT>::L * 8 * 4;
+        p.off_zk = off;
+        off += 2 * p.ngw * HB * 4;
+    }
     p.stage_bytes = static_cast<int>(align_up(off, 128));
 
     // per-warp fp16 softmax weights, then the per-warp raw accumulators
-    const int pbuf_bytes = static_cast<int>(align_up(static_cast<size_t>(kNCW) * (T / kNCW) * HB * 2, 16));
+    const int pbuf_bytes =
+        MMA ? 0 : static_cast<int>(align_up(static_cast<size_t>(kNCW) * (T / kNCW) * HB * 2, 16));
     const int abuf_bytes = kNCW * HB * kHeadDim * 4;
     // INT4 formats: per-warp score slots (one float per lane and pass group)
     constexpr int kNP = T / kNCW / 4;
     constexpr int kQG = (8 / HB) < kNP ? (8 / HB) : kNP;
-    const int sc_bytes = F::KG ? kNCW * (kNP / kQG) * 32 * 4 : 0;
+    const int sc_bytes = (F::KG && !MMA) ? kNCW * (kNP / kQG) * 32 * 4 : 0;
     const int work = pbuf_bytes + abuf_bytes + sc_bytes;
-    const int fixed = work + kNCW * HB * 3 * 4 + 80 + (3 * 8 + 2) * 8;
+    const int fixed = work + kNCW * HB * 3 * 4 + 80 + (4 * 8 + 2) * 8;
     int nst = (di.max_smem_optin - fixed - 256) / p.stage_bytes;
     nst = std::min(nst, 8);
     if (nst < 2) {
@@ -1248,6 +2088,7 @@ lik_status launch_t(const DecodeArgs& a, const DeviceInfo& di, cudaStream_t stre
     }
     // Never more stages than one CTA can use.
     p.nst = nst;
+    p.fd_nst = make_fdiv(static_cast<uint32_t>(nst));
     size_t o2 = static_cast<size_t>(nst) * p.stage_bytes;
     p.off_work = static_cast<int>(o2);
     p.off_abuf = static_cast<int>(o2 + pbuf_bytes);
@@ -1260,7 +2101,7 @@ lik_status launch_t(const DecodeArgs& a, const DeviceInfo& di, cudaStream_t stre
     o2 += 16 + sizeof(EpiDesc) + sizeof(UnitSpan);
     o2 = align_up(o2, 8);
     p.off_bar = static_cast<int>(o2);
-    o2 += (3 * nst + 2) * 8;
+    o2 += (4 * nst + 2) * 8;
     const size_t smem = o2;
 
     p.n_ctas = static_cast<int>(std::min<long long>(p.total_tiles, di.sm_count));
@@ -1276,7 +2117,7 @@ lik_status launch_t(const DecodeArgs& a, const DeviceInfo& di, cudaStream_t stre
         return LIK_ERR_WORKSPACE;
     }
 
-    auto kern = decode_kernel<FMT, HB>;
+    auto kern = decode_kernel<FMT, HB, MMA>;
     static std::once_flag once[64];
     static cudaError_t attr_err[64];
     int dev = 0;
@@ -1291,7 +2132,7 @@ lik_status launch_t(const DecodeArgs& a, const DeviceInfo& di, cudaStream_t stre
     }
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(p.n_ctas);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(threads_for<FMT, MMA>());
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -1308,16 +2149,16 @@ lik_status launch_t(const DecodeArgs& a, const DeviceInfo& di, cudaStream_t stre
     return LIK_OK;
 }
 
-template <int FMT>
+template <int FMT, bool MMA>
 lik_status launch_fmt(const DecodeArgs& a, const DeviceInfo& di, cudaStream_t s, std::string& err) {
-    switch (heads_per_unit(a.n_heads / a.n_kv_heads, FMT)) {
+    switch (heads_per_unit(a.n_heads / a.n_kv_heads, FMT, MMA)) {
         case 8:
-            if constexpr (FMT == kF16) return launch_t<FMT, 8>(a, di, s, err);
-            err = "internal: eight heads per unit is fp16-only";
+            if constexpr (FMT == kF16 || MMA) return launch_t<FMT, 8, MMA>(a, di, s, err);
+            err = "internal: eight heads per unit needs the fp16 or tensor-pipe consumer";
             return LIK_ERR_UNSUPPORTED;
-        case 4: return launch_t<FMT, 4>(a, di, s, err);
-        case 2: return launch_t<FMT, 2>(a, di, s, err);
-        default: return launch_t<FMT, 1>(a, di, s, err);
+        case 4: return launch_t<FMT, 4, MMA>(a, di, s, err);
+        case 2: return launch_t<FMT, 2, MMA>(a, di, s, err);
+        default: return launch_t<FMT, 1, MMA>(a, di, s, err);
     }
 }
 
@@ -1327,10 +2168,14 @@ lik_status launch_decode(const DecodeArgs& a, cudaStream_t stream, std::string& 
     DeviceInfo di;
     if (!device_info(di, err)) return LIK_ERR_CUDA;
     switch (a.fmt) {
-        case kF16: return launch_fmt<kF16>(a, di, stream, err);
-        case kI8: return launch_fmt<kI8>(a, di, stream, err);
-        case kI4Sym: return launch_fmt<kI4Sym>(a, di, stream, err);
-        case kI4Asym: return launch_fmt<kI4Asym>(a, di, stream, err);
+        case kF16: return launch_fmt<kF16, false>(a, di, stream, err);
+        case kI8: return launch_fmt<kI8, true>(a, di, stream, err);
+        case kI4Sym:
+            return decode_uses_mma(a.fmt, a.group_size) ? launch_fmt<kI4Sym, true>(a, di, stream, err)
+                                                        : launch_fmt<kI4Sym, false>(a, di, stream, err);
+        case kI4Asym:
+            return decode_uses_mma(a.fmt, a.group_size) ? launch_fmt<kI4Asym, true>(a, di, stream, err)
+                                                        : launch_fmt<kI4Asym, false>(a, di, stream, err);
         default: err = "unknown KV format"; return LIK_ERR_INVALID_ARGUMENT;
     }
 }

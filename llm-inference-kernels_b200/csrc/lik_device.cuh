@@ -15,7 +15,9 @@ constexpr unsigned kFull = 0xffffffffu;
 // try_wait polls it records LIK device error 1 and bails out.
 constexpr uint32_t kMaxPolls = 1u << 24;
 
-enum DeviceError : int { kDevOk = 0, kDevWaitTimeout = 1 };
+// Device error word values (workspace offset 0). kDevBadBlock: a paged block
+// table entry outside [0, num_blocks); the tile was masked, nothing read.
+enum DeviceError : int { kDevOk = 0, kDevWaitTimeout = 1, kDevBadBlock = 2 };
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -57,6 +59,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Wait for phase `parity` of `bar` to complete, polling at most kMaxPolls
 // times. Returns false on timeout (the caller records the error and leaves).
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint32_t max_polls = kMaxPolls) {
+    // rolled: an unrolled poll loop costs kilobytes of code at every wait site
+#pragma unroll 1
     for (uint32_t i = 0; i < max_polls; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
     }

@@ -31,7 +31,7 @@ struct DecodeArgs {
     // paged KV: seqlen is the maximum context length, kv_buf_len unused
     const int* block_tables = nullptr;
     const int* context_lens = nullptr;
-    int64_t block_size = 0, max_blocks = 0;
+    int64_t block_size = 0, max_blocks = 0, num_blocks = 0;
     void* workspace = nullptr;
     size_t workspace_bytes = 0;
 };
@@ -46,10 +46,21 @@ bool device_info(DeviceInfo& info, std::string& err);
 // Record the calling thread's lik_last_error() text.
 void set_last_error(const std::string& msg);
 
+// Read (and on error reset) the device error word of a decode scratch area.
+lik_status check_error_word(void* scratch, size_t scratch_bytes, cudaStream_t stream, int* device_error);
+
 // Heads handled together by one work unit (a divisor of the GQA group size).
-int heads_per_unit(int64_t group, int fmt);
+int heads_per_unit(int64_t group, int fmt, bool mma);
+// Whether the decode of this KV format / K group size runs on the tensor pipe.
+bool decode_uses_mma(int fmt, int64_t group_size);
 
 size_t decode_workspace_bytes(int64_t batch, int64_t n_heads, int64_t n_kv_heads, int sm_count);
+// Byte offset of the per-unit completion counters inside a decode workspace.
+size_t decode_counter_offset(int sm_count);
+
+// Device address and size of the allocation-free path's fixed scratch on the
+// current device (looked up once per device; nullptr + err on failure).
+void* noalloc_scratch(size_t* bytes, std::string& err);
 
 lik_status launch_decode(const DecodeArgs& a, cudaStream_t stream, std::string& err);
 

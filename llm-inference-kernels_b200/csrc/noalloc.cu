@@ -28,7 +28,9 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 
 // Device address of g_noalloc_scratch for each device ordinal, found once per
 // device (host code cannot use the symbol itself: on the host it names a
-// stand-in, not device memory).
+// stand-in, not device memory). The array needs no clearing here: a
+// __device__ array is zero when the module loads, and every call leaves its
+// counters zero again (lik_decode_noalloc_check resets it after an error).
 void* scratch_address(std::string& err) {
     static std::mutex mu;
     static void* addr[64] = {};
@@ -50,18 +52,18 @@ void* scratch_address(std::string& err) {
             err = std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e);
             return nullptr;
         }
-        // Start from a known-zero state (the kernels rely on zero counters).
-        e = cudaMemset(p, 0, kNoAllocScratchBytes);
-        if (e != cudaSuccess) {
-            err = std::string("cudaMemset: ") + cudaGetErrorString(e);
-            return nullptr;
-        }
         addr[dev] = p;
     }
     return addr[dev];
 }
 
 }  // namespace
+
+void* noalloc_scratch(size_t* bytes, std::string& err) {
+    *bytes = kNoAllocScratchBytes;
+    return scratch_address(err);
+}
+
 }  // namespace lik
 
 extern "C" lik_status lik_decode_attention_f16_noalloc(const void* q, const void* k, const void* v, void* out,
@@ -88,4 +90,19 @@ extern "C" lik_status lik_decode_attention_f16_noalloc(const void* q, const void
     }
     return lik_decode_attention_f16(q, k, v, out, batch, n_heads, n_kv_heads, head_dim, seqlen, kv_buf_len,
                                     softmax_scale, ws, kNoAllocScratchBytes, stream);
+}
+
+extern "C" lik_status lik_decode_noalloc_check(void* stream, int* device_error) {
+    using namespace lik;
+    if (device_error == nullptr) {
+        set_last_error("lik_decode_noalloc_check: device_error must be given");
+        return LIK_ERR_INVALID_ARGUMENT;
+    }
+    std::string err;
+    void* ws = scratch_address(err);
+    if (ws == nullptr) {
+        set_last_error(err);
+        return LIK_ERR_CUDA;
+    }
+    return check_error_word(ws, kNoAllocScratchBytes, static_cast<cudaStream_t>(stream), device_error);
 }

@@ -28,17 +28,53 @@ void* cur_stream() { return static_cast<void*>(at::cuda::getCurrentCUDAStream().
 // One zero-initialised workspace per (device, stream), grown on demand. Kept
 // alive for the life of the process so repeated decode steps (and CUDA-graph
 // replays) reuse it; the kernels leave it zeroed after every call.
-at::Tensor& workspace(const at::Tensor& like, size_t bytes) {
+std::mutex& ws_mutex() {
     static std::mutex mu;
+    return mu;
+}
+std::map<std::pair<int, void*>, at::Tensor>& ws_cache() {
     static std::map<std::pair<int, void*>, at::Tensor> cache;
-    std::lock_guard<std::mutex> lock(mu);
+    return cache;
+}
+
+at::Tensor& workspace(const at::Tensor& like, size_t bytes) {
+    std::lock_guard<std::mutex> lock(ws_mutex());
     auto key = std::make_pair(static_cast<int>(like.get_device()), cur_stream());
-    at::Tensor& t = cache[key];
+    at::Tensor& t = ws_cache()[key];
     if (!t.defined() || static_cast<size_t>(t.numel()) < bytes) {
         t = torch::empty({static_cast<int64_t>(bytes)}, like.options().dtype(torch::kUInt8));
         ok_or_throw(lik_workspace_init(t.data_ptr(), bytes, cur_stream()), "workspace init");
     }
     return t;
+}
+
+// Failure detection for the torch ops: read the device error word of every
+// cached workspace of the current device (synchronizing each workspace's
+// stream). A kernel whose bounded wait expired, or that met an out-of-range
+// block-table entry, left a code there and possibly unit counters that are
+// not zero; lik_workspace_check zeroes such a workspace again, and this op
+// then raises, so the failed step is reported and the next one starts clean.
+void check_device_errors() {
+    const int dev = static_cast<int>(c10::cuda::current_device());
+    std::string msg;
+    std::lock_guard<std::mutex> lock(ws_mutex());
+    for (auto& kv : ws_cache()) {
+        if (kv.first.first != dev || !kv.second.defined()) continue;
+        int code = 0;
+        const lik_status st =
+            lik_workspace_check(kv.second.data_ptr(), kv.second.numel(), kv.first.second, &code);
+        if (st != LIK_OK) msg += std::string(msg.empty() ? "" : "; ") + lik_status_string(st) + ": " + lik_last_error();
+    }
+    TORCH_CHECK(msg.empty(), "decode kernel reported a device-side error (workspace reset): ", msg);
+}
+
+// Test hook for check_device_errors: leave, in the current stream's
+// workspace, what a decode kernel whose bounded wait expired leaves (a
+// one-warp kernel whose own bounded wait runs out; no GPU fault involved).
+void selftest_leave_timeout() {
+    const auto like = torch::empty({1}, torch::TensorOptions().device(torch::kCUDA, c10::cuda::current_device()));
+    at::Tensor& ws = workspace(like, lik_decode_workspace_bytes(1, 1, 1));
+    ok_or_throw(lik_selftest_leave_timeout(64, ws.data_ptr(), ws.numel(), cur_stream()), "selftest_leave_timeout");
 }
 
 void check_cuda(const at::Tensor& t, const char* name) {
@@ -388,7 +424,8 @@ torch::Tensor paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, tor
     ok_or_throw(lik_decode_attention_paged(fmt, q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), ptr(k_scale),
                                            ptr(v_scale), ptr(k_zero), ptr(v_zero),
                                            block_tables.data_ptr<int32_t>(), context_lens.data_ptr<int32_t>(),
-                                           out.data_ptr(), q.size(0), q.size(1), hkv, 128, k_cache.size(2),
+                                           out.data_ptr(), q.size(0), q.size(1), hkv, 128, k_cache.size(0),
+                                           k_cache.size(2),
                                            block_tables.size(1), max_context_len, group_size,
                                            static_cast<float>(softmax_scale), ws.data_ptr(), ws.numel(),
                                            cur_stream()),
@@ -542,6 +579,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           "(a multiple of group_size)",
           py::arg("x"), py::arg("codes"), py::arg("scale"), py::arg("group_size"), py::arg("pos"),
           py::arg("zero") = py::none());
+    m.def("check_device_errors", &check_device_errors,
+          "Raise if a decode kernel on this device recorded a device-side error (bounded wait expired, "
+          "out-of-range block-table entry); the affected workspaces are reset first");
+    m.def("_selftest_leave_timeout", &selftest_leave_timeout,
+          "Test hook: leave a bounded-wait timeout in the current stream's workspace");
     m.def("paged_decode_attention", &paged_decode_attention,
           "Decode attention over a paged KV cache (block tables, per-sequence lengths); the format follows the "
           "cache dtype (fp16, int8 codes, packed int4; zero points given: asymmetric INT4)",

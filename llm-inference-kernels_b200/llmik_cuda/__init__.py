@@ -54,6 +54,7 @@ dequantize_int8 = _C.dequantize_int8
 paged_decode_attention = _C.paged_decode_attention
 dequantize_int4 = _C.dequantize_int4
 paged_append = _C.paged_append
+check_device_errors = _C.check_device_errors
 
 LIBRARY_PATH = _os.path.join(_here, "libllmik_b200.so")
 
@@ -63,5 +64,5 @@ __all__ = [
     "quantize_k_per_channel_groupwise_int4_asym", "quantize_v_per_token_int4_asym",
     "decode_attention_int4_asym", "quantize_per_token_into", "quantize_v_per_token_int4_into",
     "quantize_k_per_channel_groupwise_int4_into", "dequantize_int8", "dequantize_int4", "paged_decode_attention", "paged_append",
-    "LIBRARY_PATH",
+    "check_device_errors", "LIBRARY_PATH",
 ]

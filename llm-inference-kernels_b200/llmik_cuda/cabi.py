@@ -15,7 +15,7 @@ _LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libllmik_b
 LIK_OK = 0
 STATUS_NAMES = {
     0: "LIK_OK", 1: "LIK_ERR_INVALID_ARGUMENT", 2: "LIK_ERR_UNSUPPORTED", 3: "LIK_ERR_MISALIGNED",
-    4: "LIK_ERR_WORKSPACE", 5: "LIK_ERR_CUDA", 6: "LIK_ERR_DEVICE_TIMEOUT",
+    4: "LIK_ERR_WORKSPACE", 5: "LIK_ERR_CUDA", 6: "LIK_ERR_DEVICE_TIMEOUT", 7: "LIK_ERR_DEVICE_BAD_BLOCK",
 }
 
 _p, _i64, _sz, _f, _int = C.c_void_p, C.c_int64, C.c_size_t, C.c_float, C.c_int
@@ -29,6 +29,8 @@ SIGNATURES = {
     "lik_workspace_init": (_int, [_p, _sz, _p]),
     "lik_workspace_check": (_int, [_p, _sz, _p, C.POINTER(_int)]),
     "lik_selftest_bounded_wait": (_int, [_i64, C.POINTER(_int), _p]),
+    "lik_selftest_leave_timeout": (_int, [_i64, _p, _sz, _p]),
+    "lik_decode_noalloc_check": (_int, [_p, C.POINTER(_int)]),
     "lik_decode_attention_f16": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _f, _p, _sz, _p]),
     "lik_decode_attention_f16_noalloc": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _f, _p]),
     "lik_decode_attention_int8": (_int, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _f,
@@ -45,7 +47,7 @@ SIGNATURES = {
     "lik_quantize_k_per_channel_groupwise_int4_asym": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64,
                                                               _i64, _i64, _i64, _p]),
     "lik_decode_attention_paged": (_int, [_int, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64,
-                                          _i64, _i64, _i64, _i64, _f, _p, _sz, _p]),
+                                          _i64, _i64, _i64, _i64, _i64, _f, _p, _sz, _p]),
     "lik_paged_append": (_int, [_int, _p, _p, _i64, _i64, _i64, _p, _p, _p, _i64, _i64, _p]),
     "lik_dequantize_int8": (_int, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p]),
     "lik_dequantize_int4": (_int, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p]),

@@ -279,6 +279,30 @@ def dequant_kivi_asym_to_f16(kq_packed, ks, kz, vq_packed, vs, vz, group_size):
     return k, v
 
 
+# Exactly dequantized views (fp32 code * scale [+ zero], no fp16 rounding):
+# the reference's fp32 attention (reference/attention_ref.py:43-80) on the
+# quantized values themselves. The reference's CUDA INT4 kernel folds the K
+# group scale into q and never forms fp16 K
+# (kernels/attention/fused_attention_int4.cu:74-83); kernels that fold scales
+# the same way are checked against these.
+
+def dequant_int8_exact(kq, ks, vq, vs):
+    return dequantize_per_token(kq, ks), dequantize_per_token(vq, vs)
+
+
+def dequant_kivi_sym_exact(kq_packed, ks, vq_packed, vs, group_size):
+    kq = unpack_int4_signed(kq_packed)
+    vq = unpack_int4_signed(vq_packed)
+    return dequantize_per_channel_groupwise(kq, ks, group_size), dequantize_per_token(vq, vs)
+
+
+def dequant_kivi_asym_exact(kq_packed, ks, kz, vq_packed, vs, vz, group_size):
+    kq = unpack_int4_unsigned(kq_packed)
+    vq = unpack_int4_unsigned(vq_packed)
+    return (dequantize_asym_per_channel_groupwise(kq, ks, kz, group_size),
+            dequantize_asym_per_token(vq, vs, vz))
+
+
 # ---------------------------------------------------------------------------
 # Seeded synthetic inputs (benchmark configurations)
 # ---------------------------------------------------------------------------

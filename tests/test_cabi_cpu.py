@@ -16,13 +16,14 @@ def test_library_exports_every_header_function():
     for n in names:
         assert hasattr(lib, n), n
     assert set(names) == set(cabi.SIGNATURES), "ctypes signatures out of sync with include/llmik.h"
-    assert lib.lik_abi_version() == 1
+    assert lib.lik_abi_version() == 2
 
 
 def test_status_strings():
     lib = cabi.lib()
     assert lib.lik_status_string(0) == b"ok"
     assert lib.lik_status_string(6) == b"device-side wait timed out"
+    assert lib.lik_status_string(7) == b"block-table entry out of range"
 
 
 @pytest.mark.parametrize("head_dim,seqlen,buf,nh,nkv,status", [

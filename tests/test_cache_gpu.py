@@ -138,10 +138,11 @@ def test_int8_and_fp16_cache_against_oracle(L, fmt):
     k, v = torch.cat(ks, 2).numpy(), torch.cat(vs, 2).numpy()
     if fmt == "int8":
         kq, kscale, vq, vscale = O.quantize_kv_int8_per_token(k, v)
-        k, v = O.dequant_int8_to_f16(kq, kscale.astype(np.float16), vq, vscale.astype(np.float16))
+        k16, v16 = O.dequant_int8_to_f16(kq, kscale.astype(np.float16), vq, vscale.astype(np.float16))
         km, vm = cache.materialize_fp16()
-        np.testing.assert_array_equal(km.cpu().numpy(), k)
-        np.testing.assert_array_equal(vm.cpu().numpy(), v)
+        np.testing.assert_array_equal(km.cpu().numpy(), k16)
+        np.testing.assert_array_equal(vm.cpu().numpy(), v16)
+        k, v = O.dequant_int8_exact(kq, kscale.astype(np.float16), vq, vscale.astype(np.float16))
     assert_attn_close(out, O.decode_attention(q.numpy(), k, v, SCALE))
 
 

@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 import torch
 
-from lik_testutil import assert_attn_close
+from lik_testutil import assert_attn_close, attn_kv_int8, attn_kv_kivi_asym, attn_kv_kivi_sym
 from oracle import kv_oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -75,7 +75,7 @@ def test_int8(L, b, hq, hkv, s):
     kq, ks = L.quantize_per_token(k.cuda())
     vq, vs = L.quantize_per_token(v.cuda())
     out = L.decode_attention_int8(q.cuda(), kq, ks, vq, vs, SCALE)
-    kd, vd = O.dequant_int8_to_f16(kq.cpu().numpy(), ks.cpu().numpy(), vq.cpu().numpy(), vs.cpu().numpy())
+    kd, vd = attn_kv_int8(kq.cpu().numpy(), ks.cpu().numpy(), vq.cpu().numpy(), vs.cpu().numpy())
     assert_attn_close(out.cpu().numpy(), O.decode_attention(q.numpy(), kd, vd, SCALE))
 
 
@@ -86,7 +86,7 @@ def test_int4_kivi(L, b, hq, hkv, s, gs):
     kq, ks = L.quantize_k_per_channel_groupwise_int4(k.cuda(), gs)
     vq, vs = L.quantize_v_per_token_int4(v.cuda())
     out = L.decode_attention_int4(q.cuda(), kq, ks, vq, vs, gs, SCALE)
-    kd, vd = O.dequant_kivi_sym_to_f16(kq.cpu().numpy(), ks.cpu().numpy(), vq.cpu().numpy(),
+    kd, vd = attn_kv_kivi_sym(kq.cpu().numpy(), ks.cpu().numpy(), vq.cpu().numpy(),
                                        vs.cpu().numpy(), gs)
     assert_attn_close(out.cpu().numpy(), O.decode_attention(q.numpy(), kd, vd, SCALE))
 
@@ -98,7 +98,7 @@ def test_int4_asym(L, b, hq, hkv, s, gs):
     kq, ks, kz = L.quantize_k_per_channel_groupwise_int4_asym(k.cuda(), gs)
     vq, vs, vz = L.quantize_v_per_token_int4_asym(v.cuda())
     out = L.decode_attention_int4_asym(q.cuda(), kq, ks, kz, vq, vs, vz, gs, SCALE)
-    kd, vd = O.dequant_kivi_asym_to_f16(kq.cpu().numpy(), ks.cpu().numpy(), kz.cpu().numpy(),
+    kd, vd = attn_kv_kivi_asym(kq.cpu().numpy(), ks.cpu().numpy(), kz.cpu().numpy(),
                                         vq.cpu().numpy(), vs.cpu().numpy(), vz.cpu().numpy(), gs)
     assert_attn_close(out.cpu().numpy(), O.decode_attention(q.numpy(), kd, vd, SCALE))
 
@@ -120,18 +120,18 @@ def test_live_length_in_preallocated_cache(L, fmt, s, buf):
         kq, ks = L.quantize_per_token(kc)
         vq, vs = L.quantize_per_token(vc)
         out = L.decode_attention_int8(qc, kq, ks, vq, vs, SCALE, s)
-        kd, vd = O.dequant_int8_to_f16(kq.cpu().numpy(), ks.cpu().numpy(), vq.cpu().numpy(), vs.cpu().numpy())
+        kd, vd = attn_kv_int8(kq.cpu().numpy(), ks.cpu().numpy(), vq.cpu().numpy(), vs.cpu().numpy())
     elif fmt == "int4":
         kq, ks = L.quantize_k_per_channel_groupwise_int4(kc, gs)
         vq, vs = L.quantize_v_per_token_int4(vc)
         out = L.decode_attention_int4(qc, kq, ks, vq, vs, gs, SCALE, s)
-        kd, vd = O.dequant_kivi_sym_to_f16(kq.cpu().numpy(), ks.cpu().numpy(), vq.cpu().numpy(),
+        kd, vd = attn_kv_kivi_sym(kq.cpu().numpy(), ks.cpu().numpy(), vq.cpu().numpy(),
                                            vs.cpu().numpy(), gs)
     else:
         kq, ks, kz = L.quantize_k_per_channel_groupwise_int4_asym(kc, gs)
         vq, vs, vz = L.quantize_v_per_token_int4_asym(vc)
         out = L.decode_attention_int4_asym(qc, kq, ks, kz, vq, vs, vz, gs, SCALE, s)
-        kd, vd = O.dequant_kivi_asym_to_f16(kq.cpu().numpy(), ks.cpu().numpy(), kz.cpu().numpy(),
+        kd, vd = attn_kv_kivi_asym(kq.cpu().numpy(), ks.cpu().numpy(), kz.cpu().numpy(),
                                             vq.cpu().numpy(), vs.cpu().numpy(), vz.cpu().numpy(), gs)
     ref = O.decode_attention(q.numpy(), kd, vd, SCALE, seqlen=s)
     assert np.isfinite(out.cpu().numpy()).all()
@@ -145,7 +145,7 @@ def test_unaligned_token_scales_take_the_plain_load_path(L):
     kq, ks = L.quantize_per_token(k.cuda())
     vq, vs = L.quantize_per_token(v.cuda())
     out = L.decode_attention_int8(q.cuda(), kq, ks, vq, vs, SCALE)
-    kd, vd = O.dequant_int8_to_f16(kq.cpu().numpy(), ks.cpu().numpy(), vq.cpu().numpy(), vs.cpu().numpy())
+    kd, vd = attn_kv_int8(kq.cpu().numpy(), ks.cpu().numpy(), vq.cpu().numpy(), vs.cpu().numpy())
     assert_attn_close(out.cpu().numpy(), O.decode_attention(q.numpy(), kd, vd, SCALE))
 
 
@@ -173,18 +173,18 @@ def test_many_short_units_per_cta(L, fmt, b, s):
         kq, ks = L.quantize_per_token(kc)
         vq, vs = L.quantize_per_token(vc)
         run = lambda: L.decode_attention_int8(qc, kq, ks, vq, vs, SCALE)
-        kd, vd = O.dequant_int8_to_f16(kq.cpu().numpy(), ks.cpu().numpy(), vq.cpu().numpy(), vs.cpu().numpy())
+        kd, vd = attn_kv_int8(kq.cpu().numpy(), ks.cpu().numpy(), vq.cpu().numpy(), vs.cpu().numpy())
     elif fmt == "int4":
         kq, ks = L.quantize_k_per_channel_groupwise_int4(kc, 32)
         vq, vs = L.quantize_v_per_token_int4(vc)
         run = lambda: L.decode_attention_int4(qc, kq, ks, vq, vs, 32, SCALE)
-        kd, vd = O.dequant_kivi_sym_to_f16(kq.cpu().numpy(), ks.cpu().numpy(), vq.cpu().numpy(),
+        kd, vd = attn_kv_kivi_sym(kq.cpu().numpy(), ks.cpu().numpy(), vq.cpu().numpy(),
                                            vs.cpu().numpy(), 32)
     else:
         kq, ks, kz = L.quantize_k_per_channel_groupwise_int4_asym(kc, 32)
         vq, vs, vz = L.quantize_v_per_token_int4_asym(vc)
         run = lambda: L.decode_attention_int4_asym(qc, kq, ks, kz, vq, vs, vz, 32, SCALE)
-        kd, vd = O.dequant_kivi_asym_to_f16(kq.cpu().numpy(), ks.cpu().numpy(), kz.cpu().numpy(),
+        kd, vd = attn_kv_kivi_asym(kq.cpu().numpy(), ks.cpu().numpy(), kz.cpu().numpy(),
                                             vq.cpu().numpy(), vs.cpu().numpy(), vz.cpu().numpy(), 32)
     out = run()
     assert_attn_close(out.cpu().numpy(), O.decode_attention(q.numpy(), kd, vd, SCALE))

@@ -6,7 +6,7 @@ import numpy as np
 import pytest
 import torch
 
-from lik_testutil import assert_attn_close
+from lik_testutil import assert_attn_close, attn_kv_int8, attn_kv_kivi_asym, attn_kv_kivi_sym
 from oracle import kv_oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -74,7 +74,7 @@ def test_paged_matches_oracle(L, fmt, bs, gs):
         kp, table = _pagify(kq, lens, bs, perm, n_blocks)
         vp, _ = _pagify(vq, lens, bs, perm, n_blocks)
         kw = dict(k_scale=_pagify(ks, lens, bs, perm, n_blocks)[0], v_scale=_pagify(vs, lens, bs, perm, n_blocks)[0])
-        kd, vd = O.dequant_int8_to_f16(kq.cpu().numpy(), ks.cpu().numpy(), vq.cpu().numpy(), vs.cpu().numpy())
+        kd, vd = attn_kv_int8(kq.cpu().numpy(), ks.cpu().numpy(), vq.cpu().numpy(), vs.cpu().numpy())
     else:
         asym = fmt == "int4_asym"
         if asym:
@@ -89,10 +89,10 @@ def test_paged_matches_oracle(L, fmt, bs, gs):
                   group_size=gs)
         if asym:
             kw.update(k_zero=_groups_pagify(kz, lens, bs, gs, table), v_zero=_pagify(vz, lens, bs, perm, n_blocks)[0])
-            kd, vd = O.dequant_kivi_asym_to_f16(kq.cpu().numpy(), ks.cpu().numpy(), kz.cpu().numpy(),
+            kd, vd = attn_kv_kivi_asym(kq.cpu().numpy(), ks.cpu().numpy(), kz.cpu().numpy(),
                                                 vq.cpu().numpy(), vs.cpu().numpy(), vz.cpu().numpy(), gs)
         else:
-            kd, vd = O.dequant_kivi_sym_to_f16(kq.cpu().numpy(), ks.cpu().numpy(), vq.cpu().numpy(),
+            kd, vd = attn_kv_kivi_sym(kq.cpu().numpy(), ks.cpu().numpy(), vq.cpu().numpy(),
                                                vs.cpu().numpy(), gs)
     out = L.paged_decode_attention(q.cuda(), kp, vp, table.cuda(), ctx, SCALE, S, **kw).float().cpu().numpy()
     assert np.isfinite(out).all()
@@ -193,6 +193,72 @@ def test_paged_append_then_decode(L):
         xb = seqs[b].permute(1, 0, 2).unsqueeze(0).numpy()           # [1, H, l+1, 128]
         kq, kscale = O.quantize_per_token(xb, 8)
         vq, vscale = O.quantize_per_token(np.ascontiguousarray(xb[..., ::-1]), 8)
-        kd, vd = O.dequant_int8_to_f16(kq, kscale.astype(np.float16), vq, vscale.astype(np.float16))
+        kd, vd = attn_kv_int8(kq, kscale.astype(np.float16), vq, vscale.astype(np.float16))
         ref = O.decode_attention(q[b:b + 1].numpy(), kd, vd, SCALE)
         assert_attn_close(out[b:b + 1].cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("fmt", ["f16", "int4_asym"])
+def test_out_of_range_block_entry_is_masked_and_reported(L, fmt):
+    """A block-table entry outside [0, num_blocks) is never read through: the
+    tile holding it is masked, the workspace error word records it and
+    check_device_errors() raises (and resets the workspace); other sequences
+    are unaffected and the next call is clean."""
+    g = torch.Generator().manual_seed(3)
+    B, H, HQ, bs, gs = 2, 8, 32, 64, 64
+    lens = [300, 300]
+    n_blocks = 10
+    q = torch.randn(B, HQ, 128, generator=g).half()
+    k = torch.randn(B, H, 320, 128, generator=g).half()
+    v = torch.randn(B, H, 320, 128, generator=g).half()
+    perm = list(range(n_blocks))
+    ctx = torch.tensor(lens, dtype=torch.int32).cuda()
+    kw = {}
+    if fmt == "f16":
+        kp, table = _pagify(k.cuda(), lens, bs, perm, n_blocks)
+        vp, _ = _pagify(v.cuda(), lens, bs, perm, n_blocks)
+        kd, vd = k.numpy(), v.numpy()
+    else:
+        kq, ks, kz = L.quantize_k_per_channel_groupwise_int4_asym(k.cuda(), gs)
+        vq, vs, vz = L.quantize_v_per_token_int4_asym(v.cuda())
+        kp, table = _pagify(kq, lens, bs, perm, n_blocks)
+        vp, _ = _pagify(vq, lens, bs, perm, n_blocks)
+        kw = dict(k_scale=_groups_pagify(ks, lens, bs, gs, table), v_scale=_pagify(vs, lens, bs, perm, n_blocks)[0],
+                  group_size=gs, k_zero=_groups_pagify(kz, lens, bs, gs, table),
+                  v_zero=_pagify(vz, lens, bs, perm, n_blocks)[0])
+        kd, vd = attn_kv_kivi_asym(kq.cpu().numpy(), ks.cpu().numpy(), kz.cpu().numpy(),
+                                            vq.cpu().numpy(), vs.cpu().numpy(), vz.cpu().numpy(), gs)
+    L.check_device_errors()  # clean before
+    bad = table.clone()
+    bad[1, 1] = 1 << 20   # far past the cache
+    bad[1, 3] = -5
+    out = L.paged_decode_attention(q.cuda(), kp, vp, bad.cuda(), ctx, SCALE, max(lens), **kw).float().cpu().numpy()
+    ref0 = O.decode_attention(q[:1].numpy(), kd[:1], vd[:1], SCALE, seqlen=lens[0])
+    assert_attn_close(out[:1], ref0)
+    with pytest.raises(RuntimeError, match="block-table"):
+        L.check_device_errors()
+    L.check_device_errors()  # reset: clean again
+    out = L.paged_decode_attention(q.cuda(), kp, vp, table.cuda(), ctx, SCALE, max(lens), **kw).float().cpu().numpy()
+    for b in range(B):
+        assert_attn_close(out[b:b + 1], O.decode_attention(q[b:b + 1].numpy(), kd[b:b + 1], vd[b:b + 1], SCALE,
+                                                           seqlen=lens[b]))
+    L.check_device_errors()
+
+
+def test_check_device_errors_reports_and_resets_a_timeout(L):
+    """A kernel whose bounded wait ran out leaves the timeout code and a stale
+    unit counter in the stream's workspace (emulated by a self-test kernel
+    whose own wait runs out; no GPU fault). check_device_errors() raises once,
+    resets the workspace, and decode results are right afterwards."""
+    g = torch.Generator().manual_seed(4)
+    q = torch.randn(2, 32, 128, generator=g).half().cuda()
+    k = torch.randn(2, 8, 1000, 128, generator=g).half().cuda()
+    v = torch.randn(2, 8, 1000, 128, generator=g).half().cuda()
+    L.decode_attention(q, k, v, SCALE)
+    L.check_device_errors()
+    L._C._selftest_leave_timeout()
+    with pytest.raises(RuntimeError, match="wait expired"):
+        L.check_device_errors()
+    L.check_device_errors()
+    out = L.decode_attention(q, k, v, SCALE).float().cpu().numpy()
+    assert_attn_close(out, O.decode_attention(q.cpu().numpy(), k.cpu().numpy(), v.cpu().numpy(), SCALE))
