@@ -65,11 +65,10 @@ namespace lik {
 constexpr int kNCW = 8;                    // consumer warps
 constexpr int kProducerWarp = kNCW;      // issues the bulk copies
 constexpr int kEpilogueWarp = kNCW + 1;  // finishes unit segments off the streaming path
-constexpr int kScaleWarp = kNCW + 2;     // tensor-pipe INT4 path: folds K group scales into q
 constexpr int kThreads = (kNCW + 2) * 32;
 template <int FMT, bool MMA>
 constexpr int threads_for() {
-    return (MMA && (FMT == kI4Sym || FMT == kI4Asym)) ? (kNCW + 3) * 32 : kThreads;
+    return kThreads;
 }
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -762,6 +761,91 @@ __device__ __forceinline__ void pv_kstep(const uint8_t* vrow, uint32_t b0, uint3
 
 // ---- the kernel -----------------------------------------------------------
 
+// INT4 fixed-point weight preparation for one tile (tensor-pipe path), run by
+// every consumer warp on its share of the tile's (K group, head) slices:
+// w_c = q_c * softmax_scale * log2 e * k_scale[group][c] for the 128 channels,
+// as 24-bit fixed point (step = max |w| / (2^23 - 1)) split into three byte
+// limbs laid out as QK B fragments, plus the head's score constant (asym:
+// sum_c q_c z_c; sym: -8 * the fed weights' sum, cancelling the +8 code
+// offset) and step.
+template <int FMT, int HB>
+__device__ __forceinline__ void prep_int4_weights(const DecodeParams& p, const uint8_t* sb, long long t0, int ntok,
+                                                  int w, int lane, int pcb, int phf, int head, const float (&qh)[4],
+                                                  long long unit) {
+    using F = Fmt<FMT>;
+    constexpr int L = MmaFmt<FMT>::L;
+    constexpr float kFix = 8388607.f;  // 2^23 - 1
+    const long long g0 = p.fd_gs.q(t0);
+    const int ngrp = static_cast<int>(p.fd_gs.q(t0 + ntok - 1) - g0 + 1);
+    uint32_t* bw = reinterpret_cast<uint32_t*>(const_cast<uint8_t*>(sb) + p.off_w);
+    float* zk = reinterpret_cast<float*>(const_cast<uint8_t*>(sb) + p.off_zk);
+    float* dq = zk + p.ngw * HB;
+    const int r = lane >> 3, ks = (lane >> 1) & 3;
+    // slices gi * HB + head; warp w takes the ones congruent to w mod 8
+#pragma unroll 1
+    for (int gi = w / HB; gi < ngrp; gi += kNCW / HB) {
+        const __half* gsp;
+        const __half* gzp = nullptr;
+        if (p.kg_smem) {
+            gsp = reinterpret_cast<const __half*>(sb + p.off_kgs) + gi * kHeadDim;
+            if (F::ZK) gzp = reinterpret_cast<const __half*>(sb + p.off_kgz) + gi * kHeadDim;
+        } else {
+            const long long ga = g0 + gi;
+            const long long bk = p.fd_nhb.q(unit);
+            long long gb = (bk * p.ng_buf + ga) * kHeadDim;
+            if (p.paged) {
+                const long long pos = ga * p.group_size;
+                const long long sq2 = p.fd_hkv.q(bk);
+                const long long page = checked_page(p, p.block_tables[sq2 * p.max_blocks + p.fd_bs.q(pos)]);
+                gb = ((page * p.n_kv_heads + (bk - sq2 * p.n_kv_heads)) * p.fd_gs.q(p.block_size) +
+                      p.fd_gs.q(p.fd_bs.r(pos))) * kHeadDim;
+            }
+            gsp = p.ks + gb;
+            if (F::ZK) gzp = p.kz + gb;
+        }
+        float wv[4], amax = 0.f, zp = 0.f;
+        {
+            const uint4 u = *reinterpret_cast<const uint4*>(gsp + pcb);
+            const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int i2 = 0; i2 < 4; ++i2) {
+                wv[i2] = qh[i2] * half_of(uw[i2], phf);
+                amax = fmaxf(amax, fabsf(wv[i2]));
+            }
+            if (F::ZK) {
+                const uint4 uz = *reinterpret_cast<const uint4*>(gzp + pcb);
+                const uint32_t zw[4] = {uz.x, uz.y, uz.z, uz.w};
+#pragma unroll
+                for (int i2 = 0; i2 < 4; ++i2) zp = fmaf(qh[i2], half_of(zw[i2], phf), zp);
+            }
+        }
+#pragma unroll
+        for (int m = 1; m < 32; m <<= 1) amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, m));
+        const float inv = amax > 0.f ? __fdividef(kFix, amax) : 0.f;
+        const float step = amax > 0.f ? __fdividef(amax, kFix) : 0.f;
+        int wi[4];
+#pragma unroll
+        for (int i2 = 0; i2 < 4; ++i2)  // clamp: w * inv can round up to 2^23 at the maximum
+            wi[i2] = max(-8388607, min(8388607, __float2int_rn(wv[i2] * inv)));
+        uint32_t* dst = bw + ((gi * HB + head) * 4 + r) * (L * 8) + 2 * ks + phf;
+#pragma unroll
+        for (int l = 0; l < L; ++l) dst[8 * l] = pack_bytes(wi[0], wi[1], wi[2], wi[3], 8 * (L - 1 - l));
+        if (F::ZK) {
+#pragma unroll
+            for (int m = 1; m < 32; m <<= 1) zp += __shfl_xor_sync(kFull, zp, m);
+        } else {
+            int is = (wi[0] + wi[1]) + (wi[2] + wi[3]);
+#pragma unroll
+            for (int m = 1; m < 32; m <<= 1) is += __shfl_xor_sync(kFull, is, m);
+            zp = -8.f * step * static_cast<float>(is);
+        }
+        if (lane == 0) {
+            zk[gi * HB + head] = zp;
+            dq[gi * HB + head] = step;
+        }
+    }
+}
+
 template <int FMT, int HB, bool MMA>
 __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(const DecodeParams p) {
     using F = Fmt<FMT>;
@@ -785,8 +869,6 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
     // warps wrote their state) and "epi_empty" (the epilogue warp has read it)
     uint64_t* epi_full = empty + p.nst;
     uint64_t* epi_empty = epi_full + 1;
-    // tensor-pipe INT4 path: "wfull" (the scale warp wrote the stage's folded weights)
-    uint64_t* wfull = epi_empty + 1;
     volatile int* misc = reinterpret_cast<volatile int*>(smem + p.off_misc);
     EpiDesc* desc = reinterpret_cast<EpiDesc*>(smem + p.off_misc + 16);
     float* abuf = reinterpret_cast<float*>(smem + p.off_abuf);
@@ -804,8 +886,7 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
         }
         mbar_init(epi_full, kNCW);
         mbar_init(epi_empty, 1);
-        if (MMA && F::KG)
-            for (int s2 = 0; s2 < p.nst; ++s2) mbar_init(&wfull[s2], 1);
+
         misc[0] = 0;  // abort
         misc[1] = 0;  // merge ticket result
         fence_barrier_init();
@@ -1021,156 +1102,6 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
         return;
     }
 
-    // ======================= scale warp (tensor-pipe INT4) =================
-    // For every tile, fold each K group's scales into q once for all consumer
-    // warps: W[group][head][lane block r][16 + 16 half2] in the QK B-fragment order
-    // (the rounded weights, then their rounding remainders),
-    // and the group's per-head constant (asym: sum_c q_c z_c; sym: -8 sum of
-    // the fed weights), written into the stage and released on wfull[stage].
-    if constexpr (MMA && F::KG) {
-        if (warp == kScaleWarp) {
-            // lane: block lr, k-step ks, half hf -> channels c_i = 32 lr + 8 ks +
-            // hf + 2 i (i = 0..3), byte i of B register [ks][hf] of every limb
-            constexpr int L = MmaFmt<FMT>::L;
-            constexpr float kFix = 8388607.f;  // 2^23 - 1: 24-bit signed fixed point
-            const int lr = lane >> 3, ks = (lane >> 1) & 3, hf = lane & 1;
-            const int cb = 32 * lr + 8 * ks;
-            float qv[HB][4];
-#pragma unroll
-            for (int h = 0; h < HB; ++h)
-#pragma unroll
-                for (int i = 0; i < 4; ++i) qv[h][i] = 0.f;
-            int st = 0;
-            uint32_t ph = 0;
-            long long unit = p.fd_tpu.q(tb), ti = tb - unit * p.tpu, cur_unit = -1, bk = 0, seq_len = 0;
-            for (long long i = tb; i < te; ++i) {
-                if (misc[0] || !mbar_wait_bounded(&full[st], ph)) {
-                    misc[0] = 1;
-                    if (lane == 0) atomicExch(p.err, kDevWaitTimeout);
-                    break;
-                }
-                const uint8_t* sb = smem + static_cast<size_t>(st) * p.stage_bytes;
-                if (unit != cur_unit) {
-                    cur_unit = unit;
-                    bk = p.fd_nhb.q(unit);
-                    const long long b = p.fd_hkv.q(bk);
-                    seq_len = p.seqlen;
-                    if (p.paged) {
-                        const long long cl = p.ctx_lens[b];
-                        seq_len = cl < 0 ? 0 : (cl > p.seqlen ? p.seqlen : cl);
-                    }
-                    const __half* sq = reinterpret_cast<const __half*>(sb + p.off_q);
-#pragma unroll
-                    for (int h = 0; h < HB; ++h) {
-                        const uint4 u = *reinterpret_cast<const uint4*>(sq + h * kHeadDim + cb);
-                        const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-                        for (int i2 = 0; i2 < 4; ++i2) qv[h][i2] = half_of(uw[i2], hf) * p.qscale;
-                    }
-                }
-                const long long t0 = ti * T;
-                int ntok = static_cast<int>(max(0LL, min(static_cast<long long>(T), seq_len - t0)));
-                if (p.paged) ntok = *reinterpret_cast<const volatile int*>(sb + p.off_ntok);
-                if (ntok > 0) {
-                    const long long g0 = p.fd_gs.q(t0);
-                    const long long g1 = p.fd_gs.q(t0 + ntok - 1);
-                    uint32_t* bw = reinterpret_cast<uint32_t*>(smem + static_cast<size_t>(st) * p.stage_bytes + p.off_w);
-                    float* zk = reinterpret_cast<float*>(smem + static_cast<size_t>(st) * p.stage_bytes + p.off_zk);
-                    float* dq = zk + p.ngw * HB;
-#pragma unroll 1
-                    for (long long ga = g0; ga <= g1; ++ga) {
-                        const int gi = static_cast<int>(ga - g0);
-                        const __half* gsp;
-                        const __half* gzp = nullptr;
-                        if (p.kg_smem) {
-                            gsp = reinterpret_cast<const __half*>(sb + p.off_kgs) + gi * kHeadDim;
-                            if (F::ZK) gzp = reinterpret_cast<const __half*>(sb + p.off_kgz) + gi * kHeadDim;
-                        } else {
-                            long long gb = (bk * p.ng_buf + ga) * kHeadDim;
-                            if (p.paged) {
-                                const long long pos = ga * p.group_size;
-                                const long long sq2 = p.fd_hkv.q(bk);
-                                const long long page =
-                                    checked_page(p, p.block_tables[sq2 * p.max_blocks + p.fd_bs.q(pos)]);
-                                gb = ((page * p.n_kv_heads + (bk - sq2 * p.n_kv_heads)) * p.fd_gs.q(p.block_size) +
-                                      p.fd_gs.q(p.fd_bs.r(pos))) * kHeadDim;
-                            }
-                            gsp = p.ks + gb;
-                            if (F::ZK) gzp = p.kz + gb;
-                        }
-                        float sv[4], zv4[4];
-                        {
-                            const uint4 u = *reinterpret_cast<const uint4*>(gsp + cb);
-                            const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-                            for (int i2 = 0; i2 < 4; ++i2) sv[i2] = half_of(uw[i2], hf);
-                            if (F::ZK) {
-                                const uint4 uz = *reinterpret_cast<const uint4*>(gzp + cb);
-                                const uint32_t zw[4] = {uz.x, uz.y, uz.z, uz.w};
-#pragma unroll
-                                for (int i2 = 0; i2 < 4; ++i2) zv4[i2] = half_of(zw[i2], hf);
-                            }
-                        }
-                        // per-head maximum |w| sets the fixed-point step
-                        float w[HB][4], mx[HB];
-#pragma unroll
-                        for (int h = 0; h < HB; ++h) {
-                            mx[h] = 0.f;
-#pragma unroll
-                            for (int i2 = 0; i2 < 4; ++i2) {
-                                w[h][i2] = qv[h][i2] * sv[i2];
-                                mx[h] = fmaxf(mx[h], fabsf(w[h][i2]));
-                            }
-                        }
-                        int mh;
-                        const float mres = lane_reduce_scatter<HB>(mx, lane, mh, OpMax{});
-                        float zp[HB];
-                        int ip[HB];
-#pragma unroll
-                        for (int h = 0; h < HB; ++h) {
-                            const float amax = __shfl_sync(kFull, mres, lane_of_result<HB>(h));
-                            const float inv = amax > 0.f ? kFix / amax : 0.f;
-                            int wi[4];
-#pragma unroll
-                            for (int i2 = 0; i2 < 4; ++i2)  // clamp: w * inv can round up to 2^23 at the maximum
-                                wi[i2] = max(-8388607, min(8388607, __float2int_rn(w[h][i2] * inv)));
-                            uint32_t* dst = bw + ((gi * HB + h) * 4 + lr) * (L * 8) + 2 * ks + hf;
-#pragma unroll
-                            for (int l = 0; l < L; ++l) dst[8 * l] = pack_bytes(wi[0], wi[1], wi[2], wi[3], 8 * (L - 1 - l));
-                            if (F::ZK) {
-                                zp[h] = fmaf(qv[h][0], zv4[0], fmaf(qv[h][1], zv4[1], fmaf(qv[h][2], zv4[2], qv[h][3] * zv4[3])));
-                            } else {
-                                ip[h] = (wi[0] + wi[1]) + (wi[2] + wi[3]);
-                            }
-                            if (lane == 0) dq[gi * HB + h] = amax > 0.f ? amax / kFix : 0.f;
-                        }
-                        int zh;
-                        if (F::ZK) {
-                            const float zs = lane_reduce_scatter<HB>(zp, lane, zh, OpSum{});
-                            if ((lane & (32 / HB - 1)) == 0) zk[gi * HB + zh] = zs;
-                        } else {
-                            // sym: codes enter as c + 8; -8 * (step * sum of the fixed-point weights)
-                            const int zs = lane_reduce_scatter<HB>(ip, lane, zh, OpSum{});
-                            if ((lane & (32 / HB - 1)) == 0)
-                                zk[gi * HB + zh] = -8.f * (mres > 0.f ? mres / kFix : 0.f) * static_cast<float>(zs);
-                        }
-                    }
-                }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&wfull[st]);
-                if (++st == p.nst) {
-                    st = 0;
-                    ph ^= 1u;
-                }
-                if (++ti == p.tpu) {
-                    ti = 0;
-                    ++unit;
-                }
-            }
-            return;
-        }
-    }
-
     // ======================= consumer warps (tensor pipe) =================
     // A compact rolled loop over the warp's 16-position m-tiles (TW / 16 per
     // tile), software-pipelined by one m-tile: iteration k issues the QK MMAs
@@ -1223,6 +1154,15 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
         long long iunit = p.fd_tpu.q(tb), iti = tb - iunit * p.tpu, loaded_unit = -1, iseq = 0;
         long long punit = iunit, pti = iti;
         int invl = 0, igi = -1;  // warp's valid positions in the issue tile; K group loaded
+        // INT4: the tile's fixed-point weights are prepared by all consumer warps
+        // together, one (K group, head) slice per warp and pass; warp w always
+        // takes head w % HB, whose q over the lane's 4 channels it keeps here
+        // (lane: block lane / 8, k-step (lane / 2) % 4, half lane % 2 -> channels
+        // pcb + phf + 2 i)
+        const int phf = lane & 1;
+        const int pcb = 32 * (lane >> 3) + 8 * ((lane >> 1) & 3);
+        const int ph_head = w % HB;
+        float qh[4] = {0.f, 0.f, 0.f, 0.f};
         int dn[L][4];            // the issued m-tile's raw QK accumulators (one per limb)
         float zn[2], dqn[2];     // and its per-head constants / fixed-point steps
         int nrow = 0;            // its valid rows (0..16)
@@ -1243,6 +1183,7 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
             if (k < nm) {
                 const uint8_t* sb = smem + static_cast<size_t>(ist) * p.stage_bytes;
                 if (imi == 0) {
+                    const bool iunit_new = (iunit != loaded_unit);
                     if (iunit != loaded_unit) {
                         loaded_unit = iunit;
                         iseq = p.seqlen;
@@ -1287,13 +1228,25 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                             dk[1] = __shfl_sync(kFull, step, 8 * r + 4);
                         }
                     }
-                    if (!aborted && (misc[0] || !mbar_wait_bounded(&full[ist], iph) ||
-                                     (F::KG && !mbar_wait_bounded(&wfull[ist], iph))))
-                        fail();
+                    if (!aborted && (misc[0] || !mbar_wait_bounded(&full[ist], iph))) fail();
                     int ntok = static_cast<int>(max(0LL, min(static_cast<long long>(T), iseq - iti * T)));
                     if (p.paged) ntok = *reinterpret_cast<const volatile int*>(sb + p.off_ntok);
                     invl = ntok - wt0;
                     igi = -1;
+                    if constexpr (F::KG) {
+                        if (iunit_new) {
+                            // q of this warp's head arrived with the unit's first stage
+                            const uint4 u = *reinterpret_cast<const uint4*>(
+                                reinterpret_cast<const __half*>(sb + p.off_q) + ph_head * kHeadDim + pcb);
+                            const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                            for (int i2 = 0; i2 < 4; ++i2) qh[i2] = half_of(uw[i2], phf) * p.qscale;
+                        }
+                        if (!aborted && ntok > 0)
+                            prep_int4_weights<FMT, HB>(p, sb, iti * T, ntok, w, lane, pcb, phf, ph_head, qh, iunit);
+                        // every consumer warp passes here once per tile, aborted or not
+                        named_bar_sync(2, kNCW * 32);
+                    }
                 }
                 nrow = aborted ? 0 : max(0, min(16, invl - 16 * imi));
                 if (nrow > 0) {
@@ -2079,7 +2032,7 @@ lik_status launch_t(const DecodeArgs& a, const DeviceInfo& di, cudaStream_t stre
     constexpr int kQG = (8 / HB) < kNP ? (8 / HB) : kNP;
     const int sc_bytes = (F::KG && !MMA) ? kNCW * (kNP / kQG) * 32 * 4 : 0;
     const int work = pbuf_bytes + abuf_bytes + sc_bytes;
-    const int fixed = work + kNCW * HB * 3 * 4 + 80 + (4 * 8 + 2) * 8;
+    const int fixed = work + kNCW * HB * 3 * 4 + 80 + (3 * 8 + 2) * 8;
     int nst = (di.max_smem_optin - fixed - 256) / p.stage_bytes;
     nst = std::min(nst, 8);
     if (nst < 2) {
@@ -2101,7 +2054,7 @@ lik_status launch_t(const DecodeArgs& a, const DeviceInfo& di, cudaStream_t stre
     o2 += 16 + sizeof(EpiDesc) + sizeof(UnitSpan);
     o2 = align_up(o2, 8);
     p.off_bar = static_cast<int>(o2);
-    o2 += (4 * nst + 2) * 8;
+    o2 += (3 * nst + 2) * 8;
     const size_t smem = o2;
 
     p.n_ctas = static_cast<int>(std::min<long long>(p.total_tiles, di.sm_count));
