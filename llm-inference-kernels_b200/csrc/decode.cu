@@ -880,8 +880,8 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
 
     if (tid == 0) {
         for (int s = 0; s < p.nst; ++s) {
-            mbar_init(&full[s], 32);
-            mbar_init(&fullv[s], 32);
+            mbar_init(&full[s], 1);
+            mbar_init(&fullv[s], 1);
             mbar_init(&empty[s], kNCW);
         }
         mbar_init(epi_full, kNCW);
@@ -964,6 +964,8 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                     if (F::TOKV) reinterpret_cast<__half*>(sb + p.off_vs)[t] = p.vs[rowbase + t];
                     if (F::ZV) reinterpret_cast<__half*>(sb + p.off_vz)[t] = p.vz[rowbase + t];
                 }
+                // lane 0's release-arrive below publishes the other lanes' writes
+                __syncwarp();
             }
             const bool new_unit = (j == 0 || ti == 0);
             if (lane == 0 && p.paged) {
@@ -1015,7 +1017,10 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                     }
                     pos += n;
                 }
-            } else if (lane == 0) {
+            } else if (!p.paged) {
+                // One bulk copy costs the issuing thread ~200 cycles, so the
+                // tile's copies are issued by different lanes in parallel,
+                // after lane 0 has posted both barriers' transaction bytes.
                 uint32_t bytes_k = ntok * ROWB + (new_unit ? HB * kHeadDim * 2 : 0);
                 uint32_t bytes_v = ntok * ROWB;
                 int g0 = 0, ngrp = 0;
@@ -1029,31 +1034,40 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                     ngrp = g1 - g0 + 1;
                     bytes_k += (F::ZK ? 2 : 1) * ngrp * kHeadDim * 2;
                 }
-                // K side first: QK can start while V is still in flight
-                mbar_arrive_expect_tx(&full[st], bytes_k);
-                if (new_unit) {
+                // one arrival per barrier (lane 0): per-lane arrivals are
+                // serialized shared-memory atomics
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(&full[st], bytes_k);
+                    mbar_arrive_expect_tx(&fullv[st], bytes_v);
+                }
+                __syncwarp();
+                // each lane selects one of the tile's copies; one warp-wide
+                // instruction issues them all
+                const void* src = nullptr;
+                uint32_t dst_off = 0, nbytes = 0;
+                uint64_t* bar = &full[st];
+                if (lane == 0 && ntok > 0) {
+                    src = p.k + rowbase * ROWB, dst_off = 0, nbytes = ntok * ROWB;
+                } else if (lane == 1 && ntok > 0) {
+                    src = p.v + rowbase * ROWB, dst_off = p.off_v, nbytes = ntok * ROWB, bar = &fullv[st];
+                } else if (lane == 2 && new_unit) {
                     const int hb = static_cast<int>(unit - bk * p.nhb);
                     const long long b = p.fd_hkv.q(bk);
                     const long long kvh = bk - b * p.n_kv_heads;
-                    const long long qo = (b * p.n_heads + kvh * p.nhb * HB + hb * HB) * kHeadDim;
-                    bulk_g2s(sb + p.off_q, p.q + qo, HB * kHeadDim * 2, &full[st], pol);
+                    src = p.q + (b * p.n_heads + kvh * p.nhb * HB + hb * HB) * kHeadDim;
+                    dst_off = p.off_q, nbytes = HB * kHeadDim * 2;
+                } else if (F::TOKK && lane == 3 && p.tok_bulk && ntok > 0) {
+                    src = p.ks + rowbase, dst_off = p.off_ks, nbytes = n8 * 2;
+                } else if (F::KG && lane == 4 && p.kg_smem && ntok > 0) {
+                    src = p.ks + (bk * p.ng_buf + g0) * kHeadDim, dst_off = p.off_kgs, nbytes = ngrp * kHeadDim * 2;
+                } else if (F::ZK && lane == 5 && p.kg_smem && ntok > 0) {
+                    src = p.kz + (bk * p.ng_buf + g0) * kHeadDim, dst_off = p.off_kgz, nbytes = ngrp * kHeadDim * 2;
+                } else if (F::TOKV && lane == 6 && p.tok_bulk && ntok > 0) {
+                    src = p.vs + rowbase, dst_off = p.off_vs, nbytes = n8 * 2, bar = &fullv[st];
+                } else if (F::ZV && lane == 7 && p.tok_bulk && ntok > 0) {
+                    src = p.vz + rowbase, dst_off = p.off_vz, nbytes = n8 * 2, bar = &fullv[st];
                 }
-                bulk_g2s(sb, p.k + rowbase * ROWB, ntok * ROWB, &full[st], pol);
-                if (F::TOKK && p.tok_bulk) bulk_g2s(sb + p.off_ks, p.ks + rowbase, n8 * 2, &full[st], pol);
-                if (F::KG && p.kg_smem && ntok > 0) {
-                    const long long gb = (bk * p.ng_buf + g0) * kHeadDim;
-                    bulk_g2s(sb + p.off_kgs, p.ks + gb, ngrp * kHeadDim * 2, &full[st], pol);
-                    if (F::ZK) bulk_g2s(sb + p.off_kgz, p.kz + gb, ngrp * kHeadDim * 2, &full[st], pol);
-                }
-                mbar_arrive_expect_tx(&fullv[st], bytes_v);
-                bulk_g2s(sb + p.off_v, p.v + rowbase * ROWB, ntok * ROWB, &fullv[st], pol);
-                if (p.tok_bulk) {
-                    if (F::TOKV) bulk_g2s(sb + p.off_vs, p.vs + rowbase, n8 * 2, &fullv[st], pol);
-                    if (F::ZV) bulk_g2s(sb + p.off_vz, p.vz + rowbase, n8 * 2, &fullv[st], pol);
-                }
-            } else {
-                mbar_arrive(&full[st]);
-                mbar_arrive(&fullv[st]);
+                if (nbytes > 0) bulk_g2s(sb + dst_off, src, nbytes, bar, pol);
             }
             if (++st == p.nst) {
                 st = 0;
@@ -1398,14 +1412,25 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                         zv[hh] += __shfl_xor_sync(kFull, zv[hh], m);
                         lf[hh] += __shfl_xor_sync(kFull, lf[hh], m);
                     }
-                wait_handoff_free(p, epi_empty, misc, nhand, lane);
+                float* abuf_s = abuf;
+                float* mlb_s = mlb;
+                if (final_seg) {
+                    // The CTA's last segment: every tile is consumed and no copy is in
+                    // flight, so once all consumer warps are here the warp states go into
+                    // the stage memory, without waiting for the epilogue warp's hand-off.
+                    named_bar_sync(1, kNCW * 32);
+                    abuf_s = reinterpret_cast<float*>(smem);
+                    mlb_s = abuf_s + kNCW * HB * kHeadDim;
+                } else {
+                    wait_handoff_free(p, epi_empty, misc, nhand, lane);
+                }
 #pragma unroll
                 for (int hh = 0; hh < 2; ++hh) {
                     const int h = 2 * r + hh;
                     if (h < HB) {
                         if (g == 0) {
-                            mlb[(w * HB + h) * 3] = m_run[hh];
-                            mlb[(w * HB + h) * 3 + 1] = l_run[hh];
+                            mlb_s[(w * HB + h) * 3] = m_run[hh];
+                            mlb_s[(w * HB + h) * 3 + 1] = l_run[hh];
                         }
                         const float add = F::ZV ? zv[hh] : -M::VOFF * lf[hh];
                         float o[16];
@@ -1414,7 +1439,7 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                             o[2 * mt] = fmaf(acc[mt][hh], kSub, add);
                             o[2 * mt + 1] = fmaf(acc[mt][2 + hh], kScHi, add);
                         }
-                        float4* dst = reinterpret_cast<float4*>(abuf + (w * HB + h) * kHeadDim + 16 * g);
+                        float4* dst = reinterpret_cast<float4*>(abuf_s + (w * HB + h) * kHeadDim + 16 * g);
 #pragma unroll
                         for (int q4 = 0; q4 < 4; ++q4)
                             dst[q4] = make_float4(o[4 * q4], o[4 * q4 + 1], o[4 * q4 + 2], o[4 * q4 + 3]);
@@ -1428,7 +1453,7 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                 const long long qoff = (b * p.n_heads + kvh * p.nhb * HB + hb * HB) * kHeadDim;
                 finish_segment<HB>(p, final_seg, whole, punit, qoff,
                                    2 * cta + (punit == first_unit_of_cta ? 0 : 1), nhand, desc, epi_full, misc,
-                                   mlb, abuf, last_span, w, lane, tid);
+                                   mlb_s, abuf_s, last_span, w, lane, tid);
             }
             if (++pst == p.nst) {
                 pst = 0;
@@ -1855,14 +1880,25 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
 #pragma unroll
                     for (int c = 0; c < 8; ++c) acc[h][c] += __shfl_xor_sync(kFull, acc[h][c], 16);
             }
-            wait_handoff_free(p, epi_empty, misc, nhand, lane);
+            float* abuf_s = abuf;
+            float* mlb_s = mlb;
+            if (final_seg) {
+                // The CTA's last segment: every tile is consumed and no copy is in
+                // flight, so once all consumer warps are here the warp states go into
+                // the stage memory, without waiting for the epilogue warp's hand-off.
+                named_bar_sync(1, kNCW * 32);
+                abuf_s = reinterpret_cast<float*>(smem);
+                mlb_s = abuf_s + kNCW * HB * kHeadDim;
+            } else {
+                wait_handoff_free(p, epi_empty, misc, nhand, lane);
+            }
             if (grp == 0 && prim && qpl == 0) {
-                mlb[(w * HB + hh) * 3] = m_run;
-                mlb[(w * HB + hh) * 3 + 1] = l_run;
+                mlb_s[(w * HB + hh) * 3] = m_run;
+                mlb_s[(w * HB + hh) * 3 + 1] = l_run;
             }
 #pragma unroll
             for (int h = 0; h < HB; ++h) {
-                float* dst = abuf + (w * HB + h) * kHeadDim;
+                float* dst = abuf_s + (w * HB + h) * kHeadDim;
                 if (PVC == 4) {
                     *reinterpret_cast<float4*>(dst + lane * 4) =
                         make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
@@ -1882,7 +1918,7 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
 #pragma unroll
                 for (int c = 0; c < PVC; ++c) acc[h][c] = 0.f;
             finish_segment<HB>(p, final_seg, whole, unit, qoff, 2 * cta + (unit == first_unit_of_cta ? 0 : 1), nhand,
-                               desc, epi_full, misc, mlb, abuf, last_span, w, lane, tid);
+                               desc, epi_full, misc, mlb_s, abuf_s, last_span, w, lane, tid);
         }
         if (++st == p.nst) {
             st = 0;
