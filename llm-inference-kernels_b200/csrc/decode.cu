@@ -1117,10 +1117,10 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
     }
 
     // ======================= consumer warps (tensor pipe) =================
-    // A compact rolled loop over the warp's 16-position m-tiles (TW / 16 per
-    // tile), software-pipelined by one m-tile: iteration k issues the QK MMAs
-    // of m-tile k, then finishes m-tile k - 1 (scores, softmax, PV), so the QK
-    // chain of one m-tile overlaps the softmax and PV of the previous one.
+    // Per tile, each warp takes TW / 16 consecutive 16-position m-tiles and runs
+    // them side by side in one straight block: the QK MMAs of all of them, one
+    // softmax update (a single vote), then the PV MMAs of all of them, so the
+    // independent chains overlap and the tile loop carries little control flow.
     if constexpr (MMA) {
         using M = MmaFmt<FMT>;
         const int w = warp;
@@ -1128,6 +1128,7 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
         const int rg = rho(g);
         const int vr = rho(2 * r);
         constexpr int MT = TW / 16;         // m-tiles per warp per tile
+        constexpr int L = M::L;
         constexpr float kSub = 16777216.f;  // 2^24: subnormal code units
         constexpr float kScHi = M::I4 ? kSub / 16.f : kSub;  // INT4 c_hi rows were fed as 16 n
         const int wt0 = w * TW;
@@ -1138,7 +1139,6 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
 
         float acc[8][4];
         float m_run[2], l_run[2], zv[2], lf[2];
-        constexpr int L = M::L;
         uint32_t Bq[L][4][2];  // fixed-point limbs of the folded QK weights (B fragments)
         float zk[2], dk[2];    // per-head score constant and fixed-point step of the weights loaded
         bool aborted = false;
@@ -1161,13 +1161,6 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
             misc[0] = 1;
             if (lane == 0) atomicExch(p.err, kDevWaitTimeout);
         };
-
-        // issue cursor (m-tile whose QK is issued next) and process cursor
-        int ist = 0, imi = 0, pst = 0, pmi = 0;
-        uint32_t iph = 0, pph = 0;
-        long long iunit = p.fd_tpu.q(tb), iti = tb - iunit * p.tpu, loaded_unit = -1, iseq = 0;
-        long long punit = iunit, pti = iti;
-        int invl = 0, igi = -1;  // warp's valid positions in the issue tile; K group loaded
         // INT4: the tile's fixed-point weights are prepared by all consumer warps
         // together, one (K group, head) slice per warp and pass; warp w always
         // takes head w % HB, whose q over the lane's 4 channels it keeps here
@@ -1177,233 +1170,231 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
         const int pcb = 32 * (lane >> 3) + 8 * ((lane >> 1) & 3);
         const int ph_head = w % HB;
         float qh[4] = {0.f, 0.f, 0.f, 0.f};
-        int dn[L][4];            // the issued m-tile's raw QK accumulators (one per limb)
-        float zn[2], dqn[2];     // and its per-head constants / fixed-point steps
-        int nrow = 0;            // its valid rows (0..16)
-        const long long nm = (te - tb) * MT;
 
-        for (long long k = 0; k <= nm; ++k) {
-            int dc[L][4];
-            float zc[2], dqc[2];
+        int st = 0;
+        uint32_t ph = 0;
+        long long unit = p.fd_tpu.q(tb), ti = tb - unit * p.tpu, cur_unit = -1, seq_len = 0;
+        for (long long i = tb; i < te; ++i) {
+            const bool new_unit = unit != cur_unit;
+            if (new_unit) {
+                cur_unit = unit;
+                seq_len = p.seqlen;
+                if (p.paged) {
+                    const long long cl = p.ctx_lens[p.fd_hkv.q(p.fd_nhb.q(unit))];
+                    seq_len = cl < 0 ? 0 : (cl > p.seqlen ? p.seqlen : cl);
+                }
+            }
+            if (!aborted && (misc[0] || !mbar_wait_bounded(&full[st], ph))) fail();
+            const uint8_t* sb = smem + static_cast<size_t>(st) * p.stage_bytes;
+            const long long t0 = ti * T;
+            int ntok = static_cast<int>(max(0LL, min(static_cast<long long>(T), seq_len - t0)));
+            if (p.paged) ntok = *reinterpret_cast<const volatile int*>(sb + p.off_ntok);
+            if constexpr (FMT == kI8) {
+                if (new_unit) {
+                    // q * softmax_scale * log2 e for head g over the lane block's
+                    // 32 channels as 16-bit fixed point (two limbs); the step is
+                    // the head's max |w| / 32767
+                    const __half* qp =
+                        reinterpret_cast<const __half*>(sb + p.off_q) + (g < HB ? g : 0) * kHeadDim + 32 * r;
+                    float wv[32];
+                    float mxw = 0.f;
 #pragma unroll
-            for (int l = 0; l < L; ++l)
+                    for (int c4 = 0; c4 < 4; ++c4) {
+                        const uint4 u = *reinterpret_cast<const uint4*>(qp + 8 * c4);
+                        const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-                for (int c = 0; c < 4; ++c) dc[l][c] = dn[l][c];
-            zc[0] = zn[0], zc[1] = zn[1];
-            dqc[0] = dqn[0], dqc[1] = dqn[1];
-            const int crow = nrow;
-
-            // ------------- issue the QK of m-tile k -------------
-            if (k < nm) {
-                const uint8_t* sb = smem + static_cast<size_t>(ist) * p.stage_bytes;
-                if (imi == 0) {
-                    const bool iunit_new = (iunit != loaded_unit);
-                    if (iunit != loaded_unit) {
-                        loaded_unit = iunit;
-                        iseq = p.seqlen;
-                        if (p.paged) {
-                            const long long cl = p.ctx_lens[p.fd_hkv.q(p.fd_nhb.q(iunit))];
-                            iseq = cl < 0 ? 0 : (cl > p.seqlen ? p.seqlen : cl);
+                        for (int i2 = 0; i2 < 8; ++i2) {
+                            wv[8 * c4 + i2] = g < HB ? half_of(uw[i2 >> 1], i2 & 1) * p.qscale : 0.f;
+                            mxw = fmaxf(mxw, fabsf(wv[8 * c4 + i2]));
+                        }
+                    }
+                    mxw = fmaxf(mxw, __shfl_xor_sync(kFull, mxw, 1));
+                    mxw = fmaxf(mxw, __shfl_xor_sync(kFull, mxw, 2));
+                    const float inv = mxw > 0.f ? 32767.f / mxw : 0.f;
+#pragma unroll
+                    for (int k2 = 0; k2 < 4; ++k2)
+#pragma unroll
+                        for (int hf = 0; hf < 2; ++hf) {
+                            const int c0 = 8 * k2 + 4 * hf;
+                            int iv[4];
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) iv[e] = max(-32767, min(32767, __float2int_rn(wv[c0 + e] * inv)));
+                            Bq[0][k2][hf] = pack_bytes(iv[0], iv[1], iv[2], iv[3], 8);
+                            Bq[1][k2][hf] = pack_bytes(iv[0], iv[1], iv[2], iv[3], 0);
+                        }
+                    const float step = mxw > 0.f ? mxw / 32767.f : 0.f;
+                    dk[0] = __shfl_sync(kFull, step, 8 * r);
+                    dk[1] = __shfl_sync(kFull, step, 8 * r + 4);
+                }
+            }
+            if constexpr (F::KG) {
+                if (new_unit) {
+                    // q of this warp's head arrived with the unit's first stage
+                    const uint4 u = *reinterpret_cast<const uint4*>(
+                        reinterpret_cast<const __half*>(sb + p.off_q) + ph_head * kHeadDim + pcb);
+                    const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                    for (int i2 = 0; i2 < 4; ++i2) qh[i2] = half_of(uw[i2], phf) * p.qscale;
+                }
+                if (!aborted && ntok > 0)
+                    prep_int4_weights<FMT, HB>(p, sb, t0, ntok, w, lane, pcb, phf, ph_head, qh, unit);
+                // every consumer warp passes here once per tile, aborted or not
+                named_bar_sync(2, kNCW * 32);
+            }
+            const int nval = aborted ? 0 : ntok - wt0;
+            int d[MT][L][4];  // raw QK accumulators per m-tile and limb
+            float zc[MT][2], dqc[MT][2];
+            if (nval > 0) {
+                // ---------------- QK (integer tensor pipe) ----------------
+                int cur_gi = -1;
+#pragma unroll
+                for (int mi = 0; mi < MT; ++mi) {
+                    if (16 * mi < nval) {
+                        if constexpr (F::KG) {
+                            const int gi = static_cast<int>(p.fd_gs.q(t0 + wt0 + 16 * mi) - p.fd_gs.q(t0));
+                            if (gi != cur_gi) {
+                                cur_gi = gi;
+                                const uint4* bw = reinterpret_cast<const uint4*>(
+                                    sb + p.off_w + ((gi * HB + (g < HB ? g : 0)) * 4 + r) * (L * 32));
+#pragma unroll
+                                for (int l = 0; l < L; ++l) {
+                                    const uint4 u0 = bw[2 * l], u1 = bw[2 * l + 1];
+                                    const bool on = g < HB;
+                                    Bq[l][0][0] = on ? u0.x : 0u, Bq[l][0][1] = on ? u0.y : 0u;
+                                    Bq[l][1][0] = on ? u0.z : 0u, Bq[l][1][1] = on ? u0.w : 0u;
+                                    Bq[l][2][0] = on ? u1.x : 0u, Bq[l][2][1] = on ? u1.y : 0u;
+                                    Bq[l][3][0] = on ? u1.z : 0u, Bq[l][3][1] = on ? u1.w : 0u;
+                                }
+                                const float* zkp = reinterpret_cast<const float*>(sb + p.off_zk) + gi * HB;
+                                const float* dqp = zkp + p.ngw * HB;
+                                zk[0] = 2 * r < HB ? zkp[2 * r] : 0.f;
+                                zk[1] = 2 * r + 1 < HB ? zkp[2 * r + 1] : 0.f;
+                                dk[0] = 2 * r < HB ? dqp[2 * r] : 0.f;
+                                dk[1] = 2 * r + 1 < HB ? dqp[2 * r + 1] : 0.f;
+                            }
+                        }
+                        qk_mtile_int<FMT, L>(sb + (wt0 + 16 * mi + rg) * ROWB + (M::I4 ? 16 : 32) * r, Bq, d[mi]);
+                        zc[mi][0] = zk[0], zc[mi][1] = zk[1];
+                        dqc[mi][0] = dk[0], dqc[mi][1] = dk[1];
+                    }
+                }
+            }
+            // every warp waits for the stage's V copies before releasing it, also
+            // when none of its positions is live
+            if (!aborted && (misc[0] || !mbar_wait_bounded(&fullv[st], ph))) fail();
+            if (nval > 0 && !aborted) {
+                {
+                    // ---------------- scores ----------------
+                    float sc[MT][4];
+#pragma unroll
+                    for (int mi = 0; mi < MT; ++mi) {
+                        const int row = wt0 + 16 * mi + rg;
+                        const bool ok0 = 16 * mi + rg < nval, ok1 = 16 * mi + rg + 8 < nval;
+                        float dv[4];
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) {
+                            if constexpr (L == 2)
+                                dv[c] = static_cast<float>(d[mi][0][c] * 256 + d[mi][1][c]);
+                            else
+                                dv[c] = fmaf(static_cast<float>(d[mi][0][c] * 256 + d[mi][1][c]), 256.f,
+                                             static_cast<float>(d[mi][2][c]));
                         }
                         if constexpr (FMT == kI8) {
-                            if (!aborted && (misc[0] || !mbar_wait_bounded(&full[ist], iph))) fail();
-                            // q * softmax_scale * log2 e for head g over the lane block's
-                            // 32 channels as 16-bit fixed point (two limbs); the step is
-                            // the head's max |w| / 32767
-                            const __half* qp = reinterpret_cast<const __half*>(sb + p.off_q) +
-                                               (g < HB ? g : 0) * kHeadDim + 32 * r;
-                            float wv[32];
-                            float mxw = 0.f;
+                            const __half* sks = reinterpret_cast<const __half*>(sb + p.off_ks);
+                            const float k0 = __half2float(sks[row]), k1 = __half2float(sks[row + 8]);
+                            sc[mi][0] = dv[0] * dqc[mi][0] * k0;
+                            sc[mi][1] = dv[1] * dqc[mi][1] * k0;
+                            sc[mi][2] = dv[2] * dqc[mi][0] * k1;
+                            sc[mi][3] = dv[3] * dqc[mi][1] * k1;
+                        } else {
+                            sc[mi][0] = fmaf(dv[0], dqc[mi][0], zc[mi][0]);
+                            sc[mi][1] = fmaf(dv[1], dqc[mi][1], zc[mi][1]);
+                            sc[mi][2] = fmaf(dv[2], dqc[mi][0], zc[mi][0]);
+                            sc[mi][3] = fmaf(dv[3], dqc[mi][1], zc[mi][1]);
+                        }
+                        // rows past the live length (and m-tiles past it) are masked
+                        if (!ok0) sc[mi][0] = sc[mi][1] = -INFINITY;
+                        if (!ok1) sc[mi][2] = sc[mi][3] = -INFINITY;
+                    }
+                    // ---------------- online softmax (log2 domain) ----------------
+                    // The running maximum is only raised when a score exceeds it
+                    // by more than kTau (weights up to 2^kTau, which keeps
+                    // p * v_scale inside fp16 for every fp16 V): one vote.
+                    float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-                            for (int c4 = 0; c4 < 4; ++c4) {
-                                const uint4 u = *reinterpret_cast<const uint4*>(qp + 8 * c4);
-                                const __half* hv = reinterpret_cast<const __half*>(&u);
+                    for (int mi = 0; mi < MT; ++mi) {
+                        mx0 = fmaxf(mx0, fmaxf(sc[mi][0], sc[mi][2]));
+                        mx1 = fmaxf(mx1, fmaxf(sc[mi][1], sc[mi][3]));
+                    }
+                    if (__any_sync(kFull, mx0 > m_run[0] + M::kTau || mx1 > m_run[1] + M::kTau)) {
+                        mx0 = fmaxf(mx0, __shfl_xor_sync(kFull, mx0, 4));
+                        mx1 = fmaxf(mx1, __shfl_xor_sync(kFull, mx1, 4));
+                        mx0 = fmaxf(mx0, __shfl_xor_sync(kFull, mx0, 8));
+                        mx1 = fmaxf(mx1, __shfl_xor_sync(kFull, mx1, 8));
+                        mx0 = fmaxf(mx0, __shfl_xor_sync(kFull, mx0, 16));
+                        mx1 = fmaxf(mx1, __shfl_xor_sync(kFull, mx1, 16));
+                        const float mn0 = fmaxf(m_run[0], mx0), mn1 = fmaxf(m_run[1], mx1);
+                        const float a0 = mn0 == -INFINITY ? 1.f : fast_exp2(m_run[0] - mn0);
+                        const float a1 = mn1 == -INFINITY ? 1.f : fast_exp2(m_run[1] - mn1);
+                        m_run[0] = mn0;
+                        m_run[1] = mn1;
+                        l_run[0] *= a0, zv[0] *= a0, lf[0] *= a0;
+                        l_run[1] *= a1, zv[1] *= a1, lf[1] *= a1;
 #pragma unroll
-                                for (int i2 = 0; i2 < 8; ++i2) {
-                                    wv[8 * c4 + i2] = g < HB ? __half2float(hv[i2]) * p.qscale : 0.f;
-                                    mxw = fmaxf(mxw, fabsf(wv[8 * c4 + i2]));
-                                }
-                            }
-                            mxw = fmaxf(mxw, __shfl_xor_sync(kFull, mxw, 1));
-                            mxw = fmaxf(mxw, __shfl_xor_sync(kFull, mxw, 2));
-                            const float inv = mxw > 0.f ? 32767.f / mxw : 0.f;
-#pragma unroll
-                            for (int k2 = 0; k2 < 4; ++k2)
-#pragma unroll
-                                for (int hf = 0; hf < 2; ++hf) {
-                                    const int c0 = 8 * k2 + 4 * hf;
-                                    auto fx = [&](float x) { return max(-32767, min(32767, __float2int_rn(x * inv))); };
-                                    const int i0 = fx(wv[c0]), i1 = fx(wv[c0 + 1]), i2 = fx(wv[c0 + 2]), i3 = fx(wv[c0 + 3]);
-                                    Bq[0][k2][hf] = pack_bytes(i0, i1, i2, i3, 8);
-                                    Bq[1][k2][hf] = pack_bytes(i0, i1, i2, i3, 0);
-                                }
-                            const float step = mxw > 0.f ? mxw / 32767.f : 0.f;
-                            dk[0] = __shfl_sync(kFull, step, 8 * r);
-                            dk[1] = __shfl_sync(kFull, step, 8 * r + 4);
+                        for (int mt = 0; mt < 8; ++mt) {
+                            acc[mt][0] *= a0;
+                            acc[mt][1] *= a1;
+                            acc[mt][2] *= a0;
+                            acc[mt][3] *= a1;
                         }
                     }
-                    if (!aborted && (misc[0] || !mbar_wait_bounded(&full[ist], iph))) fail();
-                    int ntok = static_cast<int>(max(0LL, min(static_cast<long long>(T), iseq - iti * T)));
-                    if (p.paged) ntok = *reinterpret_cast<const volatile int*>(sb + p.off_ntok);
-                    invl = ntok - wt0;
-                    igi = -1;
-                    if constexpr (F::KG) {
-                        if (iunit_new) {
-                            // q of this warp's head arrived with the unit's first stage
-                            const uint4 u = *reinterpret_cast<const uint4*>(
-                                reinterpret_cast<const __half*>(sb + p.off_q) + ph_head * kHeadDim + pcb);
-                            const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+                    const float mu0 = m_run[0] == -INFINITY ? 0.f : m_run[0];
+                    const float mu1 = m_run[1] == -INFINITY ? 0.f : m_run[1];
+                    uint32_t bf[MT][2];
 #pragma unroll
-                            for (int i2 = 0; i2 < 4; ++i2) qh[i2] = half_of(uw[i2], phf) * p.qscale;
+                    for (int mi = 0; mi < MT; ++mi) {
+                        const int row = wt0 + 16 * mi + rg;
+                        const bool ok0 = 16 * mi + rg < nval, ok1 = 16 * mi + rg + 8 < nval;
+                        const float p0 = fast_exp2(sc[mi][0] - mu0), p1 = fast_exp2(sc[mi][1] - mu1);
+                        const float p2 = fast_exp2(sc[mi][2] - mu0), p3 = fast_exp2(sc[mi][3] - mu1);
+                        l_run[0] += p0 + p2;
+                        l_run[1] += p1 + p3;
+                        const __half* svs = reinterpret_cast<const __half*>(sb + p.off_vs);
+                        const float v0 = ok0 ? __half2float(svs[row]) : 0.f;
+                        const float v1 = ok1 ? __half2float(svs[row + 8]) : 0.f;
+                        if (F::ZV) {
+                            const __half* svz = reinterpret_cast<const __half*>(sb + p.off_vz);
+                            const float z0 = ok0 ? __half2float(svz[row]) : 0.f;
+                            const float z1 = ok1 ? __half2float(svz[row + 8]) : 0.f;
+                            zv[0] = fmaf(p0, z0, fmaf(p2, z1, zv[0]));
+                            zv[1] = fmaf(p1, z0, fmaf(p3, z1, zv[1]));
                         }
-                        if (!aborted && ntok > 0)
-                            prep_int4_weights<FMT, HB>(p, sb, iti * T, ntok, w, lane, pcb, phf, ph_head, qh, iunit);
-                        // every consumer warp passes here once per tile, aborted or not
-                        named_bar_sync(2, kNCW * 32);
-                    }
-                }
-                nrow = aborted ? 0 : max(0, min(16, invl - 16 * imi));
-                if (nrow > 0) {
-                    if constexpr (F::KG) {
-                        const long long t0 = iti * T;
-                        const int gi = static_cast<int>(p.fd_gs.q(t0 + wt0 + 16 * imi) - p.fd_gs.q(t0));
-                        if (gi != igi) {
-                            igi = gi;
-                            const uint4* bw = reinterpret_cast<const uint4*>(
-                                sb + p.off_w + ((gi * HB + (g < HB ? g : 0)) * 4 + r) * (L * 32));
-#pragma unroll
-                            for (int l = 0; l < L; ++l) {
-                                const uint4 u0 = bw[2 * l], u1 = bw[2 * l + 1];
-                                Bq[l][0][0] = u0.x, Bq[l][0][1] = u0.y, Bq[l][1][0] = u0.z, Bq[l][1][1] = u0.w;
-                                Bq[l][2][0] = u1.x, Bq[l][2][1] = u1.y, Bq[l][3][0] = u1.z, Bq[l][3][1] = u1.w;
-                            }
-                            if (g >= HB) {
-#pragma unroll
-                                for (int l = 0; l < L; ++l)
-#pragma unroll
-                                    for (int k2 = 0; k2 < 4; ++k2) Bq[l][k2][0] = Bq[l][k2][1] = 0u;
-                            }
-                            const float* zkp = reinterpret_cast<const float*>(sb + p.off_zk) + gi * HB;
-                            const float* dqp = zkp + p.ngw * HB;
-                            zk[0] = 2 * r < HB ? zkp[2 * r] : 0.f;
-                            zk[1] = 2 * r + 1 < HB ? zkp[2 * r + 1] : 0.f;
-                            dk[0] = 2 * r < HB ? dqp[2 * r] : 0.f;
-                            dk[1] = 2 * r + 1 < HB ? dqp[2 * r + 1] : 0.f;
+                        const uint32_t pr0 = pack_h2(p0 * v0, p1 * v0);
+                        const uint32_t pr1 = pack_h2(p2 * v1, p3 * v1);
+                        if (!F::ZV) {
+                            // the exact sum of the fed weights cancels the V code offset
+                            fma_h2_2acc(pr0, 0x3c003c00u, lf[0], lf[1]);
+                            fma_h2_2acc(pr1, 0x3c003c00u, lf[0], lf[1]);
                         }
+                        bf[mi][0] = movmatrix_trans(pr0);
+                        bf[mi][1] = movmatrix_trans(pr1);
                     }
-                    qk_mtile_int<FMT, L>(sb + (wt0 + 16 * imi + rg) * ROWB + (M::I4 ? 16 : 32) * r, Bq, dn);
-                    zn[0] = zk[0], zn[1] = zk[1];
-                    dqn[0] = dk[0], dqn[1] = dk[1];
-                }
-                if (++imi == MT) {
-                    imi = 0;
-                    if (++ist == p.nst) {
-                        ist = 0;
-                        iph ^= 1u;
-                    }
-                    if (++iti == p.tpu) {
-                        iti = 0;
-                        ++iunit;
-                    }
+                    // ---------------- PV (tensor pipe) ----------------
+#pragma unroll
+                    for (int mi = 0; mi < MT; ++mi)
+                        if (16 * mi < nval)
+                            pv_kstep<FMT>(sb + p.off_v + (wt0 + 16 * mi + vr) * ROWB + (M::I4 ? 8 : 16) * g,
+                                          bf[mi][0], bf[mi][1], acc);
                 }
             }
-            if (k == 0) continue;
-
-            // ------------- finish m-tile k - 1: scores, softmax, PV -------------
-            const uint8_t* sb = smem + static_cast<size_t>(pst) * p.stage_bytes;
-            if (pmi == 0 && !aborted && (misc[0] || !mbar_wait_bounded(&fullv[pst], pph))) fail();
-            if (!aborted && crow > 0) {
-                const int row = wt0 + 16 * pmi + rg;
-                const bool ok0 = rg < crow, ok1 = rg + 8 < crow;  // rows past the live length: masked
-                // raw dot products from the integer limbs (exact in fp32)
-                float dv[4];
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    if constexpr (L == 2)
-                        dv[c] = static_cast<float>(dc[0][c] * 256 + dc[1][c]);
-                    else
-                        dv[c] = fmaf(static_cast<float>(dc[0][c] * 256 + dc[1][c]), 256.f, static_cast<float>(dc[2][c]));
-                }
-                float sc[4];
-                if constexpr (FMT == kI8) {
-                    const __half* sks = reinterpret_cast<const __half*>(sb + p.off_ks);
-                    const float k0 = __half2float(sks[row]), k1 = __half2float(sks[row + 8]);
-                    sc[0] = dv[0] * dqc[0] * k0;
-                    sc[1] = dv[1] * dqc[1] * k0;
-                    sc[2] = dv[2] * dqc[0] * k1;
-                    sc[3] = dv[3] * dqc[1] * k1;
-                } else {
-                    sc[0] = fmaf(dv[0], dqc[0], zc[0]);
-                    sc[1] = fmaf(dv[1], dqc[1], zc[1]);
-                    sc[2] = fmaf(dv[2], dqc[0], zc[0]);
-                    sc[3] = fmaf(dv[3], dqc[1], zc[1]);
-                }
-                if (!ok0) sc[0] = sc[1] = -INFINITY;
-                if (!ok1) sc[2] = sc[3] = -INFINITY;
-                // Online softmax (log2 domain). The running maximum is only
-                // raised when a score exceeds it by more than kTau (weights up
-                // to 2^kTau, which keeps p * v_scale inside fp16 for every fp16
-                // V); the common case costs one vote.
-                float mx0 = fmaxf(sc[0], sc[2]), mx1 = fmaxf(sc[1], sc[3]);
-                if (__any_sync(kFull, mx0 > m_run[0] + M::kTau || mx1 > m_run[1] + M::kTau)) {
-                    mx0 = fmaxf(mx0, __shfl_xor_sync(kFull, mx0, 4));
-                    mx1 = fmaxf(mx1, __shfl_xor_sync(kFull, mx1, 4));
-                    mx0 = fmaxf(mx0, __shfl_xor_sync(kFull, mx0, 8));
-                    mx1 = fmaxf(mx1, __shfl_xor_sync(kFull, mx1, 8));
-                    mx0 = fmaxf(mx0, __shfl_xor_sync(kFull, mx0, 16));
-                    mx1 = fmaxf(mx1, __shfl_xor_sync(kFull, mx1, 16));
-                    const float mn0 = fmaxf(m_run[0], mx0), mn1 = fmaxf(m_run[1], mx1);
-                    const float a0 = mn0 == -INFINITY ? 1.f : fast_exp2(m_run[0] - mn0);
-                    const float a1 = mn1 == -INFINITY ? 1.f : fast_exp2(m_run[1] - mn1);
-                    m_run[0] = mn0;
-                    m_run[1] = mn1;
-                    l_run[0] *= a0, zv[0] *= a0, lf[0] *= a0;
-                    l_run[1] *= a1, zv[1] *= a1, lf[1] *= a1;
-#pragma unroll
-                    for (int mt = 0; mt < 8; ++mt) {
-                        acc[mt][0] *= a0;
-                        acc[mt][1] *= a1;
-                        acc[mt][2] *= a0;
-                        acc[mt][3] *= a1;
-                    }
-                }
-                const float mu0 = m_run[0] == -INFINITY ? 0.f : m_run[0];
-                const float mu1 = m_run[1] == -INFINITY ? 0.f : m_run[1];
-                const float p0 = fast_exp2(sc[0] - mu0), p1 = fast_exp2(sc[1] - mu1);
-                const float p2 = fast_exp2(sc[2] - mu0), p3 = fast_exp2(sc[3] - mu1);
-                l_run[0] += p0 + p2;
-                l_run[1] += p1 + p3;
-                const __half* svs = reinterpret_cast<const __half*>(sb + p.off_vs);
-                const float v0 = ok0 ? __half2float(svs[row]) : 0.f;
-                const float v1 = ok1 ? __half2float(svs[row + 8]) : 0.f;
-                if (F::ZV) {
-                    const __half* svz = reinterpret_cast<const __half*>(sb + p.off_vz);
-                    const float z0 = ok0 ? __half2float(svz[row]) : 0.f;
-                    const float z1 = ok1 ? __half2float(svz[row + 8]) : 0.f;
-                    zv[0] = fmaf(p0, z0, fmaf(p2, z1, zv[0]));
-                    zv[1] = fmaf(p1, z0, fmaf(p3, z1, zv[1]));
-                }
-                const uint32_t pr0 = pack_h2(p0 * v0, p1 * v0);
-                const uint32_t pr1 = pack_h2(p2 * v1, p3 * v1);
-                if (!F::ZV) {
-                    // the exact sum of the fed weights cancels the V code offset
-                    fma_h2_2acc(pr0, 0x3c003c00u, lf[0], lf[1]);
-                    fma_h2_2acc(pr1, 0x3c003c00u, lf[0], lf[1]);
-                }
-                pv_kstep<FMT>(sb + p.off_v + (wt0 + 16 * pmi + vr) * ROWB + (M::I4 ? 8 : 16) * g,
-                              movmatrix_trans(pr0), movmatrix_trans(pr1), acc);
-            }
-            if (++pmi < MT) continue;
-
-            // ------------- the tile is finished -------------
-            pmi = 0;
             __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[pst]);
-            const long long i = tb + (k - 1) / MT;
-            if (pti == p.tpu - 1 || i == te - 1) {
-                // end of a unit segment
+            if (lane == 0) mbar_arrive(&empty[st]);
+
+            // ---------------- end of a unit segment ----------------
+            if (ti == p.tpu - 1 || i == te - 1) {
                 const bool final_seg = (i == te - 1);
-                const bool whole = (pti == p.tpu - 1) && (punit * p.tpu >= tb);
+                // whole: this CTA's segment covers the unit from its first tile
+                const bool whole = (ti == p.tpu - 1) && (unit * p.tpu >= tb);
 #pragma unroll
                 for (int hh = 0; hh < 2; ++hh)
 #pragma unroll
@@ -1415,9 +1406,10 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                 float* abuf_s = abuf;
                 float* mlb_s = mlb;
                 if (final_seg) {
-                    // The CTA's last segment: every tile is consumed and no copy is in
-                    // flight, so once all consumer warps are here the warp states go into
-                    // the stage memory, without waiting for the epilogue warp's hand-off.
+                    // The CTA's last segment: every tile is consumed and no copy is
+                    // in flight, so once all consumer warps are here the warp states
+                    // go into the stage memory, without waiting for the epilogue
+                    // warp's hand-off.
                     named_bar_sync(1, kNCW * 32);
                     abuf_s = reinterpret_cast<float*>(smem);
                     mlb_s = abuf_s + kNCW * HB * kHeadDim;
@@ -1446,22 +1438,21 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                     }
                 }
                 reset_state();
-                const long long bk = p.fd_nhb.q(punit);
-                const long long hb = punit - bk * p.nhb;
+                const long long bk = p.fd_nhb.q(unit);
+                const long long hb = unit - bk * p.nhb;
                 const long long b = p.fd_hkv.q(bk);
                 const long long kvh = bk - b * p.n_kv_heads;
                 const long long qoff = (b * p.n_heads + kvh * p.nhb * HB + hb * HB) * kHeadDim;
-                finish_segment<HB>(p, final_seg, whole, punit, qoff,
-                                   2 * cta + (punit == first_unit_of_cta ? 0 : 1), nhand, desc, epi_full, misc,
-                                   mlb_s, abuf_s, last_span, w, lane, tid);
+                finish_segment<HB>(p, final_seg, whole, unit, qoff, 2 * cta + (unit == first_unit_of_cta ? 0 : 1),
+                                   nhand, desc, epi_full, misc, mlb_s, abuf_s, last_span, w, lane, tid);
             }
-            if (++pst == p.nst) {
-                pst = 0;
-                pph ^= 1u;
+            if (++st == p.nst) {
+                st = 0;
+                ph ^= 1u;
             }
-            if (++pti == p.tpu) {
-                pti = 0;
-                ++punit;
+            if (++ti == p.tpu) {
+                ti = 0;
+                ++unit;
             }
         }
         return;

@@ -1,9 +1,8 @@
 """Generate the golden vectors that pin the CPU oracle to the reference.
 
-Run where the reference checkout is available (its location is taken from
-``LLMIK_REFERENCE``, with the build container's mount point as default)::
+Run where a reference checkout is available, naming its location::
 
-    python tests/golden/make_golden.py
+    LLMIK_REFERENCE=<reference checkout> python tests/golden/make_golden.py
 
 It imports the reference's own PyTorch oracles (``reference/kv_cache_ref.py``,
 ``reference/attention_ref.py``) and its test-side INT4 unpack helper
@@ -22,7 +21,9 @@ from pathlib import Path
 import numpy as np
 import torch
 
-REF = Path(os.environ.get("LLMIK_REFERENCE", "/root/reference"))
+if not os.environ.get("LLMIK_REFERENCE"):
+    sys.exit("set LLMIK_REFERENCE to the reference checkout")
+REF = Path(os.environ["LLMIK_REFERENCE"])
 OUT = Path(__file__).resolve().parent
 
 sys.path.insert(0, str(REF))
