@@ -602,11 +602,15 @@ struct MmaFmt {
     static constexpr float VOFF = FMT == kI4Sym ? 8.f : FMT == kI8 ? 128.f : 0.f;  // V code offset
     // fixed-point limbs of the folded QK weights (INT8: 16 bits, INT4: 24 bits;
     // the INT4 weights carry the K group scale and need the wider range)
-    static constexpr int L = I4 ? 3 : 2;
+    static constexpr int L = I4 ? 3 : FMT == kI8 ? 2 : 1;
     // Softmax weights may reach 2^kTau before the running maximum is raised.
     // The fp16 weight p * v_scale stays finite for every fp16 V: v_scale is at
     // most 65504 / 127 (INT8) or 2 * 65504 / 15 (INT4), so p <= 64 resp. 4.
-    static constexpr float kTau = FMT == kI8 ? 6.f : 2.f;
+    // fp16 KV: p itself is fed (at most 2^8), the accumulators are fp32.
+    static constexpr float kTau = FMT == kI8 ? 6.f : FMT == kF16 ? 8.f : 2.f;
+    // byte offset of lane r's first K chunk and of lane g's V channels in a row
+    static constexpr int KCB = I4 ? 16 : FMT == kI8 ? 32 : 16;
+    static constexpr int VCB = I4 ? 8 : FMT == kI8 ? 16 : 32;
 };
 
 // two subnormal halves from the low (x & 0x000F000F) / high (x & 0x00F000F0)
@@ -701,6 +705,25 @@ __device__ __forceinline__ void qk_mtile_int(const uint8_t* krow, const uint32_t
     }
 }
 
+// QK of one 16-position m-tile of an fp16 K tile on the f16 tensor pipe
+// (fp32 accumulate: exact products). Lane r's channels are the 16-byte chunks
+// r, r + 4, r + 8, r + 12 of a row (krow is offset to chunk r; the four lanes
+// of a row read four different bank groups); k-step ks uses the lane's words
+// 2ks, 2ks + 1 of those 64 bytes. B[ks] is the matching fragment of q (head g).
+__device__ __forceinline__ void qk_mtile_f16(const uint8_t* krow, const uint32_t (&B)[8][2], float (&d)[4]) {
+    uint32_t w0[16], w1[16];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint4 a = *reinterpret_cast<const uint4*>(krow + 64 * j);
+        const uint4 b = *reinterpret_cast<const uint4*>(krow + 8 * 256 + 64 * j);
+        w0[4 * j] = a.x, w0[4 * j + 1] = a.y, w0[4 * j + 2] = a.z, w0[4 * j + 3] = a.w;
+        w1[4 * j] = b.x, w1[4 * j + 1] = b.y, w1[4 * j + 2] = b.z, w1[4 * j + 3] = b.w;
+    }
+    d[0] = d[1] = d[2] = d[3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) mma_f16_16816(d, w0[2 * ks], w1[2 * ks], w0[2 * ks + 1], w1[2 * ks + 1], B[ks][0], B[ks][1]);
+}
+
 // The fp16 in half `hf` (0: low, 1: high) of a packed word, as float.
 __device__ __forceinline__ float half_of(uint32_t w, int hf) {
     return __half2float(__ushort_as_half(static_cast<unsigned short>(w >> (16 * hf))));
@@ -738,6 +761,26 @@ __device__ __forceinline__ void pv_kstep(const uint8_t* vrow, uint32_t b0, uint3
                               b1);
             }
         }
+    } else if constexpr (FMT == kF16) {
+        // fp16 V: the lane's 16 channels (32 bytes) of four rows; M rows g and
+        // g + 8 of m-tile x are channels 16g + 2x and 16g + 2x + 1
+        constexpr int RB = 256;
+        uint32_t a[8], b[8], c[8], dd[8];
+#pragma unroll
+        for (int hv = 0; hv < 2; ++hv) {
+            const uint4 A = *reinterpret_cast<const uint4*>(vrow + 16 * hv);
+            const uint4 B = *reinterpret_cast<const uint4*>(vrow + 2 * RB + 16 * hv);
+            const uint4 C = *reinterpret_cast<const uint4*>(vrow + 8 * RB + 16 * hv);
+            const uint4 D = *reinterpret_cast<const uint4*>(vrow + 10 * RB + 16 * hv);
+            a[4 * hv] = A.x, a[4 * hv + 1] = A.y, a[4 * hv + 2] = A.z, a[4 * hv + 3] = A.w;
+            b[4 * hv] = B.x, b[4 * hv + 1] = B.y, b[4 * hv + 2] = B.z, b[4 * hv + 3] = B.w;
+            c[4 * hv] = C.x, c[4 * hv + 1] = C.y, c[4 * hv + 2] = C.z, c[4 * hv + 3] = C.w;
+            dd[4 * hv] = D.x, dd[4 * hv + 1] = D.y, dd[4 * hv + 2] = D.z, dd[4 * hv + 3] = D.w;
+        }
+#pragma unroll
+        for (int x = 0; x < 8; ++x)
+            mma_f16_16816(acc[x], __byte_perm(a[x], b[x], 0x5410), __byte_perm(a[x], b[x], 0x7632),
+                          __byte_perm(c[x], dd[x], 0x5410), __byte_perm(c[x], dd[x], 0x7632), b0, b1);
     } else {
         constexpr int RB = 128;
         const uint4 A = *reinterpret_cast<const uint4*>(vrow);
@@ -893,9 +936,11 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
     }
     // Programmatic dependent launch: this grid may start while the previous
     // kernel on the stream is still finishing; nothing in global memory is
-    // read or written before that kernel has completed.
-    grid_dependency_wait();
+    // read or written before that kernel has completed. The producer of a
+    // contiguous cache runs its first tile's address arithmetic first and
+    // waits right before its first global access.
     __syncthreads();
+    if (warp != kProducerWarp || p.paged) grid_dependency_wait();
 
     // ======================= producer warp ================================
     if (warp == kProducerWarp) {
@@ -957,6 +1002,7 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
             }
             const int n8 = (ntok + 7) & ~7;
 
+            if (j == 0 && !p.paged) grid_dependency_wait();
             // Scales that cannot use a bulk copy (unaligned slabs): plain loads.
             if ((F::TOKK || F::TOKV) && !p.tok_bulk && !p.paged) {
                 for (int t = lane; t < ntok; t += 32) {
@@ -965,6 +1011,15 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                     if (F::ZV) reinterpret_cast<__half*>(sb + p.off_vz)[t] = p.vz[rowbase + t];
                 }
                 // lane 0's release-arrive below publishes the other lanes' writes
+                __syncwarp();
+            }
+            if constexpr (FMT == kF16 && MMA) {
+                // fp16 V rows past the live length up to the next 16-position
+                // m-tile are fed to the PV MMA with p = 0: zero them, since
+                // 0 * (stale non-finite fp16) would not vanish
+                const int z1 = min((ntok + 15) & ~15, T);
+                for (int idx = lane; idx < (z1 - ntok) * (ROWB / 16); idx += 32)
+                    *reinterpret_cast<uint4*>(sb + p.off_v + ntok * ROWB + idx * 16) = make_uint4(0u, 0u, 0u, 0u);
                 __syncwarp();
             }
             const bool new_unit = (j == 0 || ti == 0);
@@ -1129,8 +1184,10 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
         const int vr = rho(2 * r);
         constexpr int MT = TW / 16;         // m-tiles per warp per tile
         constexpr int L = M::L;
-        constexpr float kSub = 16777216.f;  // 2^24: subnormal code units
-        constexpr float kScHi = M::I4 ? kSub / 16.f : kSub;  // INT4 c_hi rows were fed as 16 n
+        // output scale of the PV accumulators: 2^24 for codes fed as subnormals
+        // (INT4 odd channels were fed as 16 n), 1 for fp16 V
+        constexpr float kSub = FMT == kF16 ? 1.f : 16777216.f;
+        constexpr float kScHi = M::I4 ? kSub / 16.f : kSub;
         const int wt0 = w * TW;
         const long long first_unit_of_cta = p.fd_tpu.q(tb);
         long long nhand = 0;
@@ -1140,6 +1197,7 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
         float acc[8][4];
         float m_run[2], l_run[2], zv[2], lf[2];
         uint32_t Bq[L][4][2];  // fixed-point limbs of the folded QK weights (B fragments)
+        uint32_t Bh[8][2];     // fp16 KV: q of head g as B fragments (8 k-steps)
         float zk[2], dk[2];    // per-head score constant and fixed-point step of the weights loaded
         bool aborted = false;
         auto reset_state = [&]() {
@@ -1155,6 +1213,8 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
         for (int l = 0; l < L; ++l)
 #pragma unroll
             for (int k2 = 0; k2 < 4; ++k2) Bq[l][k2][0] = Bq[l][k2][1] = 0u;
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) Bh[ks][0] = Bh[ks][1] = 0u;
         zk[0] = zk[1] = dk[0] = dk[1] = 0.f;
         auto fail = [&]() {
             aborted = true;
@@ -1189,6 +1249,19 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
             const long long t0 = ti * T;
             int ntok = static_cast<int>(max(0LL, min(static_cast<long long>(T), seq_len - t0)));
             if (p.paged) ntok = *reinterpret_cast<const volatile int*>(sb + p.off_ntok);
+            if constexpr (FMT == kF16) {
+                if (new_unit) {
+                    // q of head g as given (the softmax scale is applied to the
+                    // fp32 scores), lane r's chunks r + 4j of the row
+                    const __half* qp = reinterpret_cast<const __half*>(sb + p.off_q) + (g < HB ? g : 0) * kHeadDim;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        uint4 u = *reinterpret_cast<const uint4*>(qp + 8 * (r + 4 * j));
+                        if (g >= HB) u = make_uint4(0u, 0u, 0u, 0u);
+                        Bh[2 * j][0] = u.x, Bh[2 * j][1] = u.y, Bh[2 * j + 1][0] = u.z, Bh[2 * j + 1][1] = u.w;
+                    }
+                }
+            }
             if constexpr (FMT == kI8) {
                 if (new_unit) {
                     // q * softmax_scale * log2 e for head g over the lane block's
@@ -1243,6 +1316,7 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
             }
             const int nval = aborted ? 0 : ntok - wt0;
             int d[MT][L][4];  // raw QK accumulators per m-tile and limb
+            float df[MT][4];  // fp16 KV: the QK accumulators
             float zc[MT][2], dqc[MT][2];
             if (nval > 0) {
                 // ---------------- QK (integer tensor pipe) ----------------
@@ -1273,7 +1347,10 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                                 dk[1] = 2 * r + 1 < HB ? dqp[2 * r + 1] : 0.f;
                             }
                         }
-                        qk_mtile_int<FMT, L>(sb + (wt0 + 16 * mi + rg) * ROWB + (M::I4 ? 16 : 32) * r, Bq, d[mi]);
+                        if constexpr (FMT == kF16)
+                            qk_mtile_f16(sb + (wt0 + 16 * mi + rg) * ROWB + M::KCB * r, Bh, df[mi]);
+                        else
+                            qk_mtile_int<FMT, L>(sb + (wt0 + 16 * mi + rg) * ROWB + M::KCB * r, Bq, d[mi]);
                         zc[mi][0] = zk[0], zc[mi][1] = zk[1];
                         dqc[mi][0] = dk[0], dqc[mi][1] = dk[1];
                     }
@@ -1293,13 +1370,18 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                         float dv[4];
 #pragma unroll
                         for (int c = 0; c < 4; ++c) {
-                            if constexpr (L == 2)
+                            if constexpr (FMT == kF16)
+                                dv[c] = df[mi][c];
+                            else if constexpr (L == 2)
                                 dv[c] = static_cast<float>(d[mi][0][c] * 256 + d[mi][1][c]);
                             else
                                 dv[c] = fmaf(static_cast<float>(d[mi][0][c] * 256 + d[mi][1][c]), 256.f,
                                              static_cast<float>(d[mi][2][c]));
                         }
-                        if constexpr (FMT == kI8) {
+                        if constexpr (FMT == kF16) {
+#pragma unroll
+                            for (int c = 0; c < 4; ++c) sc[mi][c] = dv[c] * p.qscale;
+                        } else if constexpr (FMT == kI8) {
                             const __half* sks = reinterpret_cast<const __half*>(sb + p.off_ks);
                             const float k0 = __half2float(sks[row]), k1 = __half2float(sks[row + 8]);
                             sc[mi][0] = dv[0] * dqc[mi][0] * k0;
@@ -1359,9 +1441,12 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                         const float p2 = fast_exp2(sc[mi][2] - mu0), p3 = fast_exp2(sc[mi][3] - mu1);
                         l_run[0] += p0 + p2;
                         l_run[1] += p1 + p3;
-                        const __half* svs = reinterpret_cast<const __half*>(sb + p.off_vs);
-                        const float v0 = ok0 ? __half2float(svs[row]) : 0.f;
-                        const float v1 = ok1 ? __half2float(svs[row + 8]) : 0.f;
+                        float v0 = 1.f, v1 = 1.f;  // fp16 V: p is fed as is (0 on masked rows)
+                        if constexpr (FMT != kF16) {
+                            const __half* svs = reinterpret_cast<const __half*>(sb + p.off_vs);
+                            v0 = ok0 ? __half2float(svs[row]) : 0.f;
+                            v1 = ok1 ? __half2float(svs[row + 8]) : 0.f;
+                        }
                         if (F::ZV) {
                             const __half* svz = reinterpret_cast<const __half*>(sb + p.off_vz);
                             const float z0 = ok0 ? __half2float(svz[row]) : 0.f;
@@ -1371,7 +1456,7 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                         }
                         const uint32_t pr0 = pack_h2(p0 * v0, p1 * v0);
                         const uint32_t pr1 = pack_h2(p2 * v1, p3 * v1);
-                        if (!F::ZV) {
+                        if (!F::ZV && FMT != kF16) {
                             // the exact sum of the fed weights cancels the V code offset
                             fma_h2_2acc(pr0, 0x3c003c00u, lf[0], lf[1]);
                             fma_h2_2acc(pr1, 0x3c003c00u, lf[0], lf[1]);
@@ -1383,7 +1468,7 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
 #pragma unroll
                     for (int mi = 0; mi < MT; ++mi)
                         if (16 * mi < nval)
-                            pv_kstep<FMT>(sb + p.off_v + (wt0 + 16 * mi + vr) * ROWB + (M::I4 ? 8 : 16) * g,
+                            pv_kstep<FMT>(sb + p.off_v + (wt0 + 16 * mi + vr) * ROWB + M::VCB * g,
                                           bf[mi][0], bf[mi][1], acc);
                 }
             }
@@ -1925,11 +2010,11 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
 
 // ---- host side ------------------------------------------------------------
 
-// INT8 and INT4 run QK / PV on the tensor pipe when no K group straddles a
-// 16-position MMA tile (INT4 group sizes that are multiples of 16); other INT4
-// group sizes and fp16 use the CUDA-core consumer.
+// fp16, INT8 and INT4 run QK / PV on the tensor pipe when no K group
+// straddles a 16-position MMA tile (INT4 group sizes that are multiples of
+// 16); other INT4 group sizes use the CUDA-core consumer.
 bool decode_uses_mma(int fmt, int64_t group_size) {
-    return fmt == kI8 || ((fmt == kI4Sym || fmt == kI4Asym) && group_size > 0 && group_size % 16 == 0);
+    return fmt == kF16 || fmt == kI8 || ((fmt == kI4Sym || fmt == kI4Asym) && group_size > 0 && group_size % 16 == 0);
 }
 
 int heads_per_unit(int64_t group, int fmt, bool mma) {
@@ -2148,7 +2233,7 @@ lik_status launch_decode(const DecodeArgs& a, cudaStream_t stream, std::string& 
     DeviceInfo di;
     if (!device_info(di, err)) return LIK_ERR_CUDA;
     switch (a.fmt) {
-        case kF16: return launch_fmt<kF16, false>(a, di, stream, err);
+        case kF16: return launch_fmt<kF16, true>(a, di, stream, err);
         case kI8: return launch_fmt<kI8, true>(a, di, stream, err);
         case kI4Sym:
             return decode_uses_mma(a.fmt, a.group_size) ? launch_fmt<kI4Sym, true>(a, di, stream, err)
