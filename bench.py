@@ -363,6 +363,23 @@ def check_against_oracle(out, q, k, v, units, what):
             raise SystemExit(f"bench: {what} output mismatch vs oracle (max err {err.max():.3e})")
 
 
+def check_c4_rows(out, args, fmt, rows, what):
+    """Config-4 rows of one rank's shard vs the CPU oracle."""
+    import numpy as np
+    from oracle import kv_oracle as O
+    for b in rows:
+        a = [x[b:b + 1].cpu().numpy() for x in args]
+        if fmt == "f16":
+            kk, vv = a[1], a[2]
+        else:   # (q, kq, ks, kz, vq, vs, vz), group size GS
+            kk, vv = O.dequant_kivi_asym_exact(a[1], a[2], a[3], a[4], a[5], a[6], GS)
+        ref = O.decode_attention(a[0], kk, vv, SCALE)
+        got = out[b:b + 1].float().cpu().numpy()
+        err = np.abs(got - ref)
+        if not (err <= 2e-3 + 1e-2 * np.abs(ref)).all():
+            raise SystemExit(f"bench: {what} row {b} mismatch vs oracle (max err {err.max():.3e})")
+
+
 def e2e_host_buffers(torch, L, dev, steps):
     """Config-1 fp16 step through the public op with pinned host inputs:
     H2D q, k, v + decode + D2H out inside the timed region."""
@@ -397,40 +414,56 @@ def e2e_host_buffers(torch, L, dev, steps):
 
 def e2e_decode_step(torch, L, dev, steps):
     """A serving-style decode step at config 1: the fp16 cache stays resident
-    in a preallocated [B, Hkv, S_max, D] buffer; each step uploads q and the new
-    token's K/V from pinned memory, writes them in place, attends over the live
-    length and reads the output back."""
+    in a preallocated [B, Hkv, S_max, D] buffer. Each step makes ONE pinned
+    H2D upload of a packed record (q, the new token's K and V, and its cache
+    slots), appends the token in place with the library's append kernel
+    (paged_append, the contiguous cache viewed as B blocks of S_max rows),
+    attends over the live length straight from the uploaded q, and reads the
+    output back. Returns (device ms per step, h2d bytes, d2h bytes)."""
     b, s = C1["batch"], C1["seqlen"]
     buf = s + steps + 8
     g = torch.Generator(device=dev).manual_seed(6)
     kc = torch.randn(b, HKV, buf, D, generator=g, device=dev).half()
     vc = torch.randn(b, HKV, buf, D, generator=g, device=dev).half()
-    qh = torch.randn(b, HQ, D).half().pin_memory()
-    nk = torch.randn(b, HKV, 1, D).half().pin_memory()
-    nv = torch.randn(b, HKV, 1, D).half().pin_memory()
+    nq, nkv = b * HQ * D * 2, b * HKV * D * 2
+    rec = nq + 2 * nkv + b * 8                       # q | k_new | v_new | slots (int64)
+    host = [torch.empty(rec, dtype=torch.uint8).pin_memory() for _ in range(2)]
+    for h in host:
+        h[:nq + 2 * nkv].view(torch.float16).copy_(torch.randn((nq + 2 * nkv) // 2).half())
+    dev_rec = torch.empty(rec, dtype=torch.uint8, device=dev)
+    q = dev_rec[:nq].view(torch.float16).view(b, HQ, D)
+    kn = dev_rec[nq:nq + nkv].view(torch.float16).view(b, HKV, D)
+    vn = dev_rec[nq + nkv:nq + 2 * nkv].view(torch.float16).view(b, HKV, D)
+    slots = dev_rec[nq + 2 * nkv:].view(torch.int64)
     oh = torch.empty(b, HQ, D, dtype=torch.float16).pin_memory()
-    qd = torch.empty(b, HQ, D, dtype=torch.float16, device=dev)
-    pos = [s - 1]
+    base = torch.arange(b, dtype=torch.int64) * buf
 
-    def step():
-        p = pos[0]
-        qd.copy_(qh, non_blocking=True)
-        kc[:, :, p:p + 1].copy_(nk, non_blocking=True)
-        vc[:, :, p:p + 1].copy_(nv, non_blocking=True)
-        out = L.decode_attention(qd, kc, vc, SCALE, p + 1)
+    sent = [torch.cuda.Event(), torch.cuda.Event()]
+
+    def step(p, i):
+        # double-buffered host records: the host waits only until the upload
+        # that last used this buffer (two steps back) has been consumed
+        h = host[i & 1]
+        sent[i & 1].synchronize()
+        h[nq + 2 * nkv:].view(torch.int64).copy_(base + p)
+        dev_rec.copy_(h, non_blocking=True)
+        sent[i & 1].record()
+        L.paged_append(kn, slots, kc.view(b, HKV, buf, D))
+        L.paged_append(vn, slots, vc.view(b, HKV, buf, D))
+        out = L.decode_attention(q, kc, vc, SCALE, p + 1)
         oh.copy_(out, non_blocking=True)
 
-    for _ in range(3):
-        step()
+    p = s - 1
+    for i in range(3):
+        step(p, i)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(steps):
-        step()
-        pos[0] += 1
+    for i in range(steps):
+        step(p + i, i)
     e1.record()
     torch.cuda.synchronize()
-    return e0.elapsed_time(e1) / steps
+    return e0.elapsed_time(e1) / steps, rec, oh.numel() * 2
 
 
 def time_kv_kernels(torch, L, dev, l2, peak_gbs, launches=50):
@@ -503,7 +536,6 @@ def run_ours(args):
     dist = None
     if world > 1:
         import torch.distributed as dist
-        os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep stdout to the one JSON line
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local if world > 1 else 0)
@@ -555,18 +587,21 @@ def run_ours(args):
             ms = max_over_ranks(torch, time_graph(torch, wl, c4steps, warmup, barrier, min_warm_s=0.5), world)
             c4[name] = {"us_per_step": ms * 1e3, "TB_s": world * nb / (ms * 1e-3) / 1e12,
                         "steps": c4steps, "batch_per_gpu": bl}
-            if fmt == "f16":
-                # assemble the output shards (NCCL all-gather, off the timed path)
-                # and check the last sequence against the oracle on rank 0
+            # every rank checks the first, middle and last sequence of its own
+            # shard against the CPU oracle (INT4: on the exactly dequantized KV
+            # the tensor-pipe kernel attends over)
+            out0 = wl.step(0)
+            rows = sorted({0, bl // 2, bl - 1})
+            check_c4_rows(out0, wl.sets[0], fmt, rows, f"config-4 {name} rank {rank}")
+            c4[name]["verified"] = (f"sequences {rows} of every rank's shard vs CPU oracle "
+                                    f"(global batch rows {[rank * bl + r for r in rows]} on this rank)")
+            if fmt == "f16" and world > 1:
+                # the assembled output (NCCL all-gather, off the timed path)
+                # equals the shards
                 from llmik_cuda.shard import gather_shards
-                full = gather_shards(wl.step(0))
-                if rank == 0:
-                    bl_last = C4["batch"] - 1
-                    kk, vv = make_slabs(torch, dev, 1, C4["seqlen"], bl_last * HKV, 2000, False)
-                    gq = torch.Generator(device=dev).manual_seed(2000 + 7 * 10**6 + (world - 1) * bl * HKV)
-                    qq = torch.randn(bl, HQ, D, generator=gq, device=dev).half()[-1:]
-                    check_against_oracle(full[-1:], qq, kk, vv, [0], "config-4 fp16 (gathered)")
-                    c4[name]["verified"] = "last sequence of the gathered output vs CPU oracle"
+                full = gather_shards(out0)
+                if not torch.equal(full[rank * bl:(rank + 1) * bl], out0):
+                    raise SystemExit("bench: gathered config-4 output differs from the local shard")
             del wl
             torch.cuda.empty_cache()
     peak, peak_kind = measured_hbm_peak()
@@ -577,8 +612,8 @@ def run_ours(args):
     e2e_steps = 3 if args.profile else max(3, min(steps, 20))
     e2e_ms, h2d, d2h = e2e_host_buffers(torch, L, dev, e2e_steps)
     e2e_ms = max_over_ranks(torch, e2e_ms, world)
-    dec_ms = max_over_ranks(torch, e2e_decode_step(torch, L, dev, 3 if args.profile else max(10, min(steps, 200))),
-                            world)
+    dec_ms, dec_h2d, dec_d2h = e2e_decode_step(torch, L, dev, 3 if args.profile else max(10, min(steps, 200)))
+    dec_ms = max_over_ranks(torch, dec_ms, world)
 
     nb1 = algo_bytes("f16", b, s)
     value = world * nb1 / (head_ms * 1e-3) / 1e12
@@ -597,14 +632,24 @@ def run_ours(args):
         "tokens_per_s": world * b / (head_ms * 1e-3),
         "formats": formats,
         "config4_sharded": c4,
+        # config 4 is the strong-scaling workload: global batch 64 is split
+        # over the N GPUs, so its per-N device time is the scaling curve
+        "strong_scaling": {
+            "workload": "config4: batch 64 (global) x seqlen 32768, 32 q / 8 kv heads, sharded by "
+                        "(batch, kv-head), no collective on the timed path",
+            "n_gpus": world,
+            **{f"{k}_us_per_step": v["us_per_step"] for k, v in c4.items()},
+            **{f"{k}_TB_s": v["TB_s"] for k, v in c4.items()}},
         "kv_kernels": kv_kernels,
         "e2e": {"value": world * nb1 / (e2e_ms * 1e-3) / 1e12, "unit": "TB/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
                 "what": "llmik_cuda.decode_attention with q, k, v copied from pinned host memory "
                         "and the output copied back, every step"},
-        "e2e_decode_step": {"us_per_step": dec_ms * 1e3,
-                            "what": "resident fp16 cache; per step H2D q + new K/V token, in-place "
-                                    "append, decode over the live length, D2H output"},
+        "e2e_decode_step": {"us_per_step": dec_ms * 1e3, "overhead_us_vs_kernel": (dec_ms - head_ms) * 1e3,
+                            "h2d_bytes_per_step": dec_h2d, "d2h_bytes_per_step": dec_d2h,
+                            "what": "resident fp16 cache; per step one packed pinned H2D record (q, new "
+                                    "K/V token, slots), paged_append of K and V in place, decode over the "
+                                    "live length, D2H output"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": ncu_traffic(), "peak_source": peak_kind,
                      "kernel": "decode_kernel<fp16, 4 heads/unit>"},

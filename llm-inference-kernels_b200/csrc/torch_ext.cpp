@@ -89,8 +89,47 @@ void check_q(const at::Tensor& q) {
     TORCH_CHECK(q.size(2) == 128, "only head_dim=128 supported");
 }
 
-void check_kv4(const at::Tensor& t, const char* name, at::ScalarType dt, int64_t last) {
-    check_cuda(t, name);
+// Length of the buffer a [batch, heads, seq, inner...] tensor is a prefix of:
+// the tensor is either contiguous or a view t = buffer[:, :, :n] of a
+// contiguous [batch, heads, buf, inner...] buffer (the layout a preallocated
+// cache hands out), so the rows of one (batch, head) start buf rows apart.
+int64_t seq_buffer(const at::Tensor& t, const char* name) {
+    TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+    TORCH_CHECK(t.dim() >= 3, name, " must have [batch, heads, seq, ...] dimensions");
+    const char* msg = " must be contiguous or a sequence prefix of a contiguous buffer";
+    int64_t inner = 1;
+    for (int64_t d = t.dim() - 1; d >= 3; --d) {
+        TORCH_CHECK(t.size(d) == 1 || t.stride(d) == inner, name, msg);
+        inner *= t.size(d);
+    }
+    TORCH_CHECK(t.size(2) <= 1 || t.stride(2) == inner, name, msg);
+    int64_t buf = t.size(2);
+    if (t.size(1) > 1) {
+        TORCH_CHECK(t.stride(1) % inner == 0 && t.stride(1) / inner >= t.size(2), name, msg);
+        buf = t.stride(1) / inner;
+    } else if (t.size(0) > 1) {
+        TORCH_CHECK(t.stride(0) % inner == 0 && t.stride(0) / inner >= t.size(2), name, msg);
+        buf = t.stride(0) / inner;
+    }
+    TORCH_CHECK(t.size(0) <= 1 || t.size(1) <= 1 || t.stride(0) == t.size(1) * buf * inner, name, msg);
+    return buf;
+}
+
+// The common buffer length of a call's per-position tensors (codes and
+// per-token scales share one row index).
+int64_t kv_buffer(std::initializer_list<std::pair<const at::Tensor*, const char*>> ts) {
+    int64_t buf = -1;
+    for (const auto& t : ts) {
+        const int64_t b = seq_buffer(*t.first, t.second);
+        TORCH_CHECK(buf < 0 || b == buf, t.second, " is a prefix of a buffer of another length than the K codes");
+        buf = b;
+    }
+    return buf;
+}
+
+void check_kv4(const at::Tensor& t, const char* name, at::ScalarType dt, int64_t last, bool view_ok = false) {
+    TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+    TORCH_CHECK(view_ok || t.is_contiguous(), name, " must be contiguous");
     TORCH_CHECK(t.scalar_type() == dt, name, " has the wrong dtype");
     TORCH_CHECK(t.dim() == 4, name, " must be [batch, n_kv_heads, seqlen, ", last, "]");
     TORCH_CHECK(t.size(3) == last, name, " last dim must be ", last);
@@ -111,16 +150,18 @@ void check_heads(const at::Tensor& q, const at::Tensor& k) {
     TORCH_CHECK(k.size(1) > 0 && q.size(1) % k.size(1) == 0, "n_heads must be a multiple of n_kv_heads");
 }
 
-void check_tok_scale(const at::Tensor& s, const at::Tensor& codes, const char* name) {
-    check_cuda(s, name);
+void check_tok_scale(const at::Tensor& s, const at::Tensor& codes, const char* name, bool view_ok = false) {
+    TORCH_CHECK(s.is_cuda(), name, " must be a CUDA tensor");
+    TORCH_CHECK(view_ok || s.is_contiguous(), name, " must be contiguous");
     TORCH_CHECK(s.scalar_type() == torch::kHalf, name, " must be fp16");
     TORCH_CHECK(s.dim() == 3 && s.size(0) == codes.size(0) && s.size(1) == codes.size(1) &&
                     s.size(2) == codes.size(2),
                 name, " must be [batch, n_kv_heads, seqlen]");
 }
 
-void check_group_scale(const at::Tensor& s, const at::Tensor& codes, const char* name) {
-    check_cuda(s, name);
+void check_group_scale(const at::Tensor& s, const at::Tensor& codes, const char* name, bool view_ok = false) {
+    TORCH_CHECK(s.is_cuda(), name, " must be a CUDA tensor");
+    TORCH_CHECK(view_ok || s.is_contiguous(), name, " must be contiguous");
     TORCH_CHECK(s.scalar_type() == torch::kHalf, name, " must be fp16");
     TORCH_CHECK(s.dim() == 4 && s.size(0) == codes.size(0) && s.size(1) == codes.size(1) && s.size(3) == 128,
                 name, " must be [batch, n_kv_heads, n_groups, head_dim]");
@@ -131,15 +172,15 @@ void check_group_scale(const at::Tensor& s, const at::Tensor& codes, const char*
 torch::Tensor decode_attention(torch::Tensor q, torch::Tensor k, torch::Tensor v, double softmax_scale,
                                int64_t seqlen) {
     check_q(q);
-    check_kv4(k, "k", torch::kHalf, 128);
-    check_kv4(v, "v", torch::kHalf, 128);
+    check_kv4(k, "k", torch::kHalf, 128, true);
+    check_kv4(v, "v", torch::kHalf, 128, true);
     TORCH_CHECK(k.sizes() == v.sizes(), "k and v must have the same shape");
     check_same_device(q, k);
     check_same_device(q, v);
     check_heads(q, k);
     const c10::cuda::CUDAGuard guard(q.device());
-    const int64_t buf = k.size(2);
-    const int64_t s = live_len(seqlen, buf);
+    const int64_t buf = kv_buffer({{&k, "k"}, {&v, "v"}});
+    const int64_t s = live_len(seqlen, k.size(2));
     auto out = torch::empty_like(q);
     const size_t wb = lik_decode_workspace_bytes(q.size(0), q.size(1), k.size(1));
     at::Tensor& ws = workspace(q, wb);
@@ -160,16 +201,16 @@ torch::Tensor decode_attention_v3(torch::Tensor q, torch::Tensor k, torch::Tenso
 torch::Tensor decode_attention_int8(torch::Tensor q, torch::Tensor k_q, torch::Tensor k_scale, torch::Tensor v_q,
                                     torch::Tensor v_scale, double softmax_scale, int64_t seqlen) {
     check_q(q);
-    check_kv4(k_q, "k_q", torch::kInt8, 128);
-    check_kv4(v_q, "v_q", torch::kInt8, 128);
+    check_kv4(k_q, "k_q", torch::kInt8, 128, true);
+    check_kv4(v_q, "v_q", torch::kInt8, 128, true);
     TORCH_CHECK(k_q.sizes() == v_q.sizes(), "k_q and v_q must have the same shape");
-    check_tok_scale(k_scale, k_q, "k_scale");
-    check_tok_scale(v_scale, v_q, "v_scale");
+    check_tok_scale(k_scale, k_q, "k_scale", true);
+    check_tok_scale(v_scale, v_q, "v_scale", true);
     for (auto* t : {&k_q, &v_q, &k_scale, &v_scale}) check_same_device(q, *t);
     check_heads(q, k_q);
     const c10::cuda::CUDAGuard guard(q.device());
-    const int64_t buf = k_q.size(2);
-    const int64_t s = live_len(seqlen, buf);
+    const int64_t buf = kv_buffer({{&k_q, "k_q"}, {&v_q, "v_q"}, {&k_scale, "k_scale"}, {&v_scale, "v_scale"}});
+    const int64_t s = live_len(seqlen, k_q.size(2));
     auto out = torch::empty_like(q);
     at::Tensor& ws = workspace(q, lik_decode_workspace_bytes(q.size(0), q.size(1), k_q.size(1)));
     ok_or_throw(lik_decode_attention_int8(q.data_ptr(), k_q.data_ptr<int8_t>(), k_scale.data_ptr(),
@@ -185,22 +226,23 @@ torch::Tensor decode_attention_int4(torch::Tensor q, torch::Tensor k_q, torch::T
                                     torch::Tensor v_scale, int64_t group_size, double softmax_scale,
                                     int64_t seqlen) {
     check_q(q);
-    check_kv4(k_q, "k_q", torch::kInt8, 64);
-    check_kv4(v_q, "v_q", torch::kInt8, 64);
+    check_kv4(k_q, "k_q", torch::kInt8, 64, true);
+    check_kv4(v_q, "v_q", torch::kInt8, 64, true);
     TORCH_CHECK(k_q.sizes() == v_q.sizes(), "k_q and v_q must have the same shape");
-    check_group_scale(k_scale, k_q, "k_scale");
-    check_tok_scale(v_scale, v_q, "v_scale");
+    check_group_scale(k_scale, k_q, "k_scale", true);
+    check_tok_scale(v_scale, v_q, "v_scale", true);
     TORCH_CHECK(group_size > 0, "group_size must be positive");
     for (auto* t : {&k_q, &v_q, &k_scale, &v_scale}) check_same_device(q, *t);
     check_heads(q, k_q);
     const c10::cuda::CUDAGuard guard(q.device());
-    const int64_t buf = k_q.size(2);
-    const int64_t s = live_len(seqlen, buf);
+    const int64_t buf = kv_buffer({{&k_q, "k_q"}, {&v_q, "v_q"}, {&v_scale, "v_scale"}});
+    const int64_t gbuf = seq_buffer(k_scale, "k_scale");
+    const int64_t s = live_len(seqlen, k_q.size(2));
     auto out = torch::empty_like(q);
     at::Tensor& ws = workspace(q, lik_decode_workspace_bytes(q.size(0), q.size(1), k_q.size(1)));
     ok_or_throw(lik_decode_attention_int4(q.data_ptr(), k_q.data_ptr<int8_t>(), k_scale.data_ptr(),
                                           v_q.data_ptr<int8_t>(), v_scale.data_ptr(), out.data_ptr(), q.size(0),
-                                          q.size(1), k_q.size(1), q.size(2), s, buf, group_size, k_scale.size(2),
+                                          q.size(1), k_q.size(1), q.size(2), s, buf, group_size, gbuf,
                                           static_cast<float>(softmax_scale), ws.data_ptr(), ws.numel(),
                                           cur_stream()),
                 "decode_attention_int4");
@@ -212,26 +254,28 @@ torch::Tensor decode_attention_int4_asym(torch::Tensor q, torch::Tensor k_q, tor
                                          torch::Tensor v_zero, int64_t group_size, double softmax_scale,
                                          int64_t seqlen) {
     check_q(q);
-    check_kv4(k_q, "k_q", torch::kInt8, 64);
-    check_kv4(v_q, "v_q", torch::kInt8, 64);
+    check_kv4(k_q, "k_q", torch::kInt8, 64, true);
+    check_kv4(v_q, "v_q", torch::kInt8, 64, true);
     TORCH_CHECK(k_q.sizes() == v_q.sizes(), "k_q and v_q must have the same shape");
-    check_group_scale(k_scale, k_q, "k_scale");
-    check_group_scale(k_zero, k_q, "k_zero");
+    check_group_scale(k_scale, k_q, "k_scale", true);
+    check_group_scale(k_zero, k_q, "k_zero", true);
     TORCH_CHECK(k_zero.sizes() == k_scale.sizes(), "k_zero must match k_scale");
-    check_tok_scale(v_scale, v_q, "v_scale");
-    check_tok_scale(v_zero, v_q, "v_zero");
+    check_tok_scale(v_scale, v_q, "v_scale", true);
+    check_tok_scale(v_zero, v_q, "v_zero", true);
     TORCH_CHECK(group_size > 0, "group_size must be positive");
     for (auto* t : {&k_q, &v_q, &k_scale, &v_scale, &k_zero, &v_zero}) check_same_device(q, *t);
     check_heads(q, k_q);
     const c10::cuda::CUDAGuard guard(q.device());
-    const int64_t buf = k_q.size(2);
-    const int64_t s = live_len(seqlen, buf);
+    const int64_t buf = kv_buffer({{&k_q, "k_q"}, {&v_q, "v_q"}, {&v_scale, "v_scale"}, {&v_zero, "v_zero"}});
+    const int64_t gbuf = seq_buffer(k_scale, "k_scale");
+    TORCH_CHECK(seq_buffer(k_zero, "k_zero") == gbuf, "k_zero and k_scale must share one buffer layout");
+    const int64_t s = live_len(seqlen, k_q.size(2));
     auto out = torch::empty_like(q);
     at::Tensor& ws = workspace(q, lik_decode_workspace_bytes(q.size(0), q.size(1), k_q.size(1)));
     ok_or_throw(lik_decode_attention_int4_asym(
                     q.data_ptr(), k_q.data_ptr<int8_t>(), k_scale.data_ptr(), k_zero.data_ptr(),
                     v_q.data_ptr<int8_t>(), v_scale.data_ptr(), v_zero.data_ptr(), out.data_ptr(), q.size(0),
-                    q.size(1), k_q.size(1), q.size(2), s, buf, group_size, k_scale.size(2),
+                    q.size(1), k_q.size(1), q.size(2), s, buf, group_size, gbuf,
                     static_cast<float>(softmax_scale), ws.data_ptr(), ws.numel(), cur_stream()),
                 "decode_attention_int4_asym");
     return out;

@@ -65,6 +65,9 @@ class QuantizedKVCache:
         self.fmt, self.group_size = fmt, group_size
         self.device = torch.device(device) if device is not None else torch.device("cuda")
         self.layers = [self._alloc() for _ in range(num_layers)]
+        # positions the next attention call covers (set by every append), the
+        # attribute the reference's PreallocCache hands its decode hook
+        self.cur_attn_len = 0
 
     # ---- allocation ----------------------------------------------------
     def _alloc(self) -> _Layer:
@@ -134,6 +137,7 @@ class QuantizedKVCache:
             _C.quantize_v_per_token_int4_into(v, L.v, L.vs, pos, L.vz)
             self._append_k_int4(L, k, v)
         L.n += n_new
+        self.cur_attn_len = L.n
 
     def _append_k_int4(self, L: _Layer, k: torch.Tensor, v: torch.Tensor) -> None:
         gs = self.group_size
@@ -218,3 +222,40 @@ class QuantizedKVCache:
             k[:, :, nq:] = L.kres[:, :, :L.nres]
             v[:, :, nq:] = L.vres[:, :, :L.nres]
         return k, v
+
+    # ---- the reference caches' method names ------------------------------
+    # Int4KIVICache (integration/kv_int4_cache.py:85-160,174-206) and
+    # PreallocCache (integration/prealloc_cache.py:42-78) callers use these.
+    def append_only(self, key_states: torch.Tensor, value_states: torch.Tensor, layer_idx: int) -> None:
+        """Int4KIVICache.append_only: store [batch, n_kv_heads, n_new, 128]
+        fp16 K/V without producing fp16 K/V."""
+        self.append(key_states, value_states, layer_idx)
+
+    def get_quantized_for_attention(self, layer_idx: int):
+        """Int4KIVICache.get_quantized_for_attention: the codes and scales of
+        every stored position, ready for the decode op ("int4":
+        (k_packed, k_scale, v_packed, v_scale); "int4_asym" adds (k_zero,
+        v_zero); "int8": (k_q, k_scale, v_q, v_scale)). The tensors are
+        sequence-prefix views of the preallocated buffers, which the decode
+        ops accept as they are: nothing is concatenated or copied."""
+        if self.fmt == "fp16":
+            raise RuntimeError("an fp16 cache holds no quantized tensors")
+        return self.quantized_view(layer_idx)
+
+    def get_seq_length(self, layer_idx: int = 0) -> int:
+        return self.seq_length(layer_idx)
+
+    def update(self, key_states: torch.Tensor, value_states: torch.Tensor, layer_idx: int,
+               cache_kwargs=None) -> Tuple[torch.Tensor, torch.Tensor]:
+        """The HF cache contract. fp16 cache: PreallocCache.update (prefill
+        returns its own K/V; a one-token decode step returns the whole buffers,
+        whose live prefix ``cur_attn_len`` the decode hook attends over).
+        Quantized caches: Int4KIVICache.update (append, then fp16 K/V of all
+        stored positions)."""
+        self.append(key_states, value_states, layer_idx)
+        if self.fmt == "fp16":
+            if key_states.shape[2] > 1:
+                return key_states, value_states
+            L = self.layers[layer_idx]
+            return L.k, L.v
+        return self.materialize_fp16(layer_idx)

@@ -103,6 +103,25 @@ def test_int4_asym(L, b, hq, hkv, s, gs):
     assert_attn_close(out.cpu().numpy(), O.decode_attention(q.numpy(), kd, vd, SCALE))
 
 
+@pytest.mark.parametrize("fmt", ["f16", "int4_asym"])
+def test_config4_context_length(L, fmt):
+    """Config 4's 32768-position context (3 sequences of a rank's shard; the
+    full 64-sequence shape is checked row by row inside bench.py)."""
+    b, hq, hkv, s, gs = 3, 32, 8, 32768, 128
+    q, k, v = _inputs(b, hq, hkv, s, seed=4444, k_outliers=fmt != "f16")
+    qc, kc, vc = q.cuda(), k.cuda(), v.cuda()
+    if fmt == "f16":
+        out = L.decode_attention(qc, kc, vc, SCALE)
+        kd, vd = k.numpy(), v.numpy()
+    else:
+        kq, ks, kz = L.quantize_k_per_channel_groupwise_int4_asym(kc, gs)
+        vq, vs, vz = L.quantize_v_per_token_int4_asym(vc)
+        out = L.decode_attention_int4_asym(qc, kq, ks, kz, vq, vs, vz, gs, SCALE)
+        kd, vd = attn_kv_kivi_asym(kq.cpu().numpy(), ks.cpu().numpy(), kz.cpu().numpy(),
+                                   vq.cpu().numpy(), vs.cpu().numpy(), vz.cpu().numpy(), gs)
+    assert_attn_close(out.cpu().numpy(), O.decode_attention(q.numpy(), kd, vd, SCALE))
+
+
 @pytest.mark.parametrize("fmt", ["f16", "int8", "int4", "int4_asym"])
 @pytest.mark.parametrize("s,buf", [(1, 64), (100, 256), (1000, 1003), (4095, 4096)])
 def test_live_length_in_preallocated_cache(L, fmt, s, buf):
