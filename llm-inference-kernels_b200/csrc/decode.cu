@@ -590,6 +590,19 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
     return as_u32(__floats2half2_rn(lo, hi));
 }
 
+// A consumer's wait for a stage: one poll when the stage has landed (the
+// common case, no other access); otherwise bounded polling that also gives up
+// as soon as another warp has flagged an abort in misc[0].
+__device__ __forceinline__ bool stage_wait(uint64_t* bar, uint32_t parity, volatile int* misc) {
+    if (mbar_try_wait(bar, parity)) return true;
+#pragma unroll 1
+    for (uint32_t i = 0; i < kMaxPolls; ++i) {
+        if (misc[0]) return false;
+        if (mbar_try_wait(bar, parity)) return true;
+    }
+    return false;
+}
+
 // rho: the row permutation of a 16-row MMA tile (swap bits 0 and 1)
 __device__ __forceinline__ int rho(int i) { return (i & ~3) | ((i & 1) << 1) | ((i & 2) >> 1); }
 
@@ -729,11 +742,10 @@ __device__ __forceinline__ float half_of(uint32_t w, int hf) {
     return __half2float(__ushort_as_half(static_cast<unsigned short>(w >> (16 * hf))));
 }
 
-// Pack byte `shift` of four 32-bit values into one register (value i ->
-// byte i).
-__device__ __forceinline__ uint32_t pack_bytes(int v0, int v1, int v2, int v3, int shift) {
-    const uint32_t lo = __byte_perm(static_cast<uint32_t>(v0) >> shift, static_cast<uint32_t>(v1) >> shift, 0x0040);
-    const uint32_t hi = __byte_perm(static_cast<uint32_t>(v2) >> shift, static_cast<uint32_t>(v3) >> shift, 0x0040);
+// Byte b of each of four 32-bit values, packed (value i -> byte i).
+__device__ __forceinline__ uint32_t byte_lane(int v0, int v1, int v2, int v3, int b) {
+    const uint32_t lo = __byte_perm(static_cast<uint32_t>(v0), static_cast<uint32_t>(v1), b | ((4 + b) << 4));
+    const uint32_t hi = __byte_perm(static_cast<uint32_t>(v2), static_cast<uint32_t>(v3), b | ((4 + b) << 4));
     return __byte_perm(lo, hi, 0x5410);
 }
 
@@ -862,8 +874,8 @@ __device__ __forceinline__ void prep_int4_weights(const DecodeParams& p, const u
                 for (int i2 = 0; i2 < 4; ++i2) zp = fmaf(qh[i2], half_of(zw[i2], phf), zp);
             }
         }
-#pragma unroll
-        for (int m = 1; m < 32; m <<= 1) amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, m));
+        // one warp reduction instruction: non-negative floats order like their bits
+        amax = __uint_as_float(__reduce_max_sync(kFull, __float_as_uint(amax)));
         const float inv = amax > 0.f ? __fdividef(kFix, amax) : 0.f;
         const float step = amax > 0.f ? __fdividef(amax, kFix) : 0.f;
         int wi[4];
@@ -872,14 +884,12 @@ __device__ __forceinline__ void prep_int4_weights(const DecodeParams& p, const u
             wi[i2] = max(-8388607, min(8388607, __float2int_rn(wv[i2] * inv)));
         uint32_t* dst = bw + ((gi * HB + head) * 4 + r) * (L * 8) + 2 * ks + phf;
 #pragma unroll
-        for (int l = 0; l < L; ++l) dst[8 * l] = pack_bytes(wi[0], wi[1], wi[2], wi[3], 8 * (L - 1 - l));
+        for (int l = 0; l < L; ++l) dst[8 * l] = byte_lane(wi[0], wi[1], wi[2], wi[3], L - 1 - l);
         if (F::ZK) {
 #pragma unroll
             for (int m = 1; m < 32; m <<= 1) zp += __shfl_xor_sync(kFull, zp, m);
         } else {
-            int is = (wi[0] + wi[1]) + (wi[2] + wi[3]);
-#pragma unroll
-            for (int m = 1; m < 32; m <<= 1) is += __shfl_xor_sync(kFull, is, m);
+            const int is = __reduce_add_sync(kFull, (wi[0] + wi[1]) + (wi[2] + wi[3]));
             zp = -8.f * step * static_cast<float>(is);
         }
         if (lane == 0) {
@@ -1189,6 +1199,8 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
         constexpr float kSub = FMT == kF16 ? 1.f : 16777216.f;
         constexpr float kScHi = M::I4 ? kSub / 16.f : kSub;
         const int wt0 = w * TW;
+        // INT4: a warp's TW positions of a tile lie in one K group
+        const bool one_group = F::KG && p.group_size % TW == 0;
         const long long first_unit_of_cta = p.fd_tpu.q(tb);
         long long nhand = 0;
         UnitSpan* last_span = reinterpret_cast<UnitSpan*>(smem + p.off_misc + 16 + sizeof(EpiDesc));
@@ -1244,7 +1256,7 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                     seq_len = cl < 0 ? 0 : (cl > p.seqlen ? p.seqlen : cl);
                 }
             }
-            if (!aborted && (misc[0] || !mbar_wait_bounded(&full[st], ph))) fail();
+            if (!aborted && !stage_wait(&full[st], ph, misc)) fail();
             const uint8_t* sb = smem + static_cast<size_t>(st) * p.stage_bytes;
             const long long t0 = ti * T;
             int ntok = static_cast<int>(max(0LL, min(static_cast<long long>(T), seq_len - t0)));
@@ -1292,8 +1304,8 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                             int iv[4];
 #pragma unroll
                             for (int e = 0; e < 4; ++e) iv[e] = max(-32767, min(32767, __float2int_rn(wv[c0 + e] * inv)));
-                            Bq[0][k2][hf] = pack_bytes(iv[0], iv[1], iv[2], iv[3], 8);
-                            Bq[1][k2][hf] = pack_bytes(iv[0], iv[1], iv[2], iv[3], 0);
+                            Bq[0][k2][hf] = byte_lane(iv[0], iv[1], iv[2], iv[3], 1);
+                            Bq[1][k2][hf] = byte_lane(iv[0], iv[1], iv[2], iv[3], 0);
                         }
                     const float step = mxw > 0.f ? mxw / 32767.f : 0.f;
                     dk[0] = __shfl_sync(kFull, step, 8 * r);
@@ -1315,163 +1327,174 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                 named_bar_sync(2, kNCW * 32);
             }
             const int nval = aborted ? 0 : ntok - wt0;
-            int d[MT][L][4];  // raw QK accumulators per m-tile and limb
-            float df[MT][4];  // fp16 KV: the QK accumulators
-            float zc[MT][2], dqc[MT][2];
-            if (nval > 0) {
-                // ---------------- QK (integer tensor pipe) ----------------
-                int cur_gi = -1;
-#pragma unroll
-                for (int mi = 0; mi < MT; ++mi) {
-                    if (16 * mi < nval) {
-                        if constexpr (F::KG) {
-                            const int gi = static_cast<int>(p.fd_gs.q(t0 + wt0 + 16 * mi) - p.fd_gs.q(t0));
-                            if (gi != cur_gi) {
-                                cur_gi = gi;
-                                const uint4* bw = reinterpret_cast<const uint4*>(
-                                    sb + p.off_w + ((gi * HB + (g < HB ? g : 0)) * 4 + r) * (L * 32));
-#pragma unroll
-                                for (int l = 0; l < L; ++l) {
-                                    const uint4 u0 = bw[2 * l], u1 = bw[2 * l + 1];
-                                    const bool on = g < HB;
-                                    Bq[l][0][0] = on ? u0.x : 0u, Bq[l][0][1] = on ? u0.y : 0u;
-                                    Bq[l][1][0] = on ? u0.z : 0u, Bq[l][1][1] = on ? u0.w : 0u;
-                                    Bq[l][2][0] = on ? u1.x : 0u, Bq[l][2][1] = on ? u1.y : 0u;
-                                    Bq[l][3][0] = on ? u1.z : 0u, Bq[l][3][1] = on ? u1.w : 0u;
+            // The common case, every position of the warp's share live, runs a
+            // copy of the tile body without the per-row masking.
+            auto tile_body = [&](auto full_tag) {
+                constexpr bool FULL = decltype(full_tag)::value;
+                int d[MT][L][4];  // raw QK accumulators per m-tile and limb
+                float df[MT][4];  // fp16 KV: the QK accumulators
+                float zc[MT][2], dqc[MT][2];
+                if (FULL || nval > 0) {
+                    // ---------------- QK (integer tensor pipe) ----------------
+                    int cur_gi = -1;
+    #pragma unroll
+                    for (int mi = 0; mi < MT; ++mi) {
+                        if (FULL || 16 * mi < nval) {
+                            if constexpr (F::KG) {
+                              if (mi == 0 || !one_group) {
+                                const int gi = static_cast<int>(p.fd_gs.q(t0 + wt0 + 16 * mi) - p.fd_gs.q(t0));
+                                if (gi != cur_gi) {
+                                    cur_gi = gi;
+                                    const uint4* bw = reinterpret_cast<const uint4*>(
+                                        sb + p.off_w + ((gi * HB + (g < HB ? g : 0)) * 4 + r) * (L * 32));
+    #pragma unroll
+                                    for (int l = 0; l < L; ++l) {
+                                        const uint4 u0 = bw[2 * l], u1 = bw[2 * l + 1];
+                                        const bool on = g < HB;
+                                        Bq[l][0][0] = on ? u0.x : 0u, Bq[l][0][1] = on ? u0.y : 0u;
+                                        Bq[l][1][0] = on ? u0.z : 0u, Bq[l][1][1] = on ? u0.w : 0u;
+                                        Bq[l][2][0] = on ? u1.x : 0u, Bq[l][2][1] = on ? u1.y : 0u;
+                                        Bq[l][3][0] = on ? u1.z : 0u, Bq[l][3][1] = on ? u1.w : 0u;
+                                    }
+                                    const float* zkp = reinterpret_cast<const float*>(sb + p.off_zk) + gi * HB;
+                                    const float* dqp = zkp + p.ngw * HB;
+                                    zk[0] = 2 * r < HB ? zkp[2 * r] : 0.f;
+                                    zk[1] = 2 * r + 1 < HB ? zkp[2 * r + 1] : 0.f;
+                                    dk[0] = 2 * r < HB ? dqp[2 * r] : 0.f;
+                                    dk[1] = 2 * r + 1 < HB ? dqp[2 * r + 1] : 0.f;
                                 }
-                                const float* zkp = reinterpret_cast<const float*>(sb + p.off_zk) + gi * HB;
-                                const float* dqp = zkp + p.ngw * HB;
-                                zk[0] = 2 * r < HB ? zkp[2 * r] : 0.f;
-                                zk[1] = 2 * r + 1 < HB ? zkp[2 * r + 1] : 0.f;
-                                dk[0] = 2 * r < HB ? dqp[2 * r] : 0.f;
-                                dk[1] = 2 * r + 1 < HB ? dqp[2 * r + 1] : 0.f;
+                              }
+                            }
+                            if constexpr (FMT == kF16)
+                                qk_mtile_f16(sb + (wt0 + 16 * mi + rg) * ROWB + M::KCB * r, Bh, df[mi]);
+                            else
+                                qk_mtile_int<FMT, L>(sb + (wt0 + 16 * mi + rg) * ROWB + M::KCB * r, Bq, d[mi]);
+                            zc[mi][0] = zk[0], zc[mi][1] = zk[1];
+                            dqc[mi][0] = dk[0], dqc[mi][1] = dk[1];
+                        }
+                    }
+                }
+                // every warp waits for the stage's V copies before releasing it, also
+                // when none of its positions is live
+                if (!aborted && !stage_wait(&fullv[st], ph, misc)) fail();
+                if ((FULL || nval > 0) && !aborted) {
+                    {
+                        // ---------------- scores ----------------
+                        float sc[MT][4];
+    #pragma unroll
+                        for (int mi = 0; mi < MT; ++mi) {
+                            const int row = wt0 + 16 * mi + rg;
+                            const bool ok0 = FULL || 16 * mi + rg < nval, ok1 = FULL || 16 * mi + rg + 8 < nval;
+                            float dv[4];
+    #pragma unroll
+                            for (int c = 0; c < 4; ++c) {
+                                if constexpr (FMT == kF16)
+                                    dv[c] = df[mi][c];
+                                else if constexpr (L == 2)
+                                    dv[c] = static_cast<float>(d[mi][0][c] * 256 + d[mi][1][c]);
+                                else
+                                    dv[c] = fmaf(static_cast<float>(d[mi][0][c] * 256 + d[mi][1][c]), 256.f,
+                                                 static_cast<float>(d[mi][2][c]));
+                            }
+                            if constexpr (FMT == kF16) {
+    #pragma unroll
+                                for (int c = 0; c < 4; ++c) sc[mi][c] = dv[c] * p.qscale;
+                            } else if constexpr (FMT == kI8) {
+                                const __half* sks = reinterpret_cast<const __half*>(sb + p.off_ks);
+                                const float k0 = __half2float(sks[row]), k1 = __half2float(sks[row + 8]);
+                                sc[mi][0] = dv[0] * dqc[mi][0] * k0;
+                                sc[mi][1] = dv[1] * dqc[mi][1] * k0;
+                                sc[mi][2] = dv[2] * dqc[mi][0] * k1;
+                                sc[mi][3] = dv[3] * dqc[mi][1] * k1;
+                            } else {
+                                sc[mi][0] = fmaf(dv[0], dqc[mi][0], zc[mi][0]);
+                                sc[mi][1] = fmaf(dv[1], dqc[mi][1], zc[mi][1]);
+                                sc[mi][2] = fmaf(dv[2], dqc[mi][0], zc[mi][0]);
+                                sc[mi][3] = fmaf(dv[3], dqc[mi][1], zc[mi][1]);
+                            }
+                            // rows past the live length (and m-tiles past it) are masked
+                            if (!ok0) sc[mi][0] = sc[mi][1] = -INFINITY;
+                            if (!ok1) sc[mi][2] = sc[mi][3] = -INFINITY;
+                        }
+                        // ---------------- online softmax (log2 domain) ----------------
+                        // The running maximum is only raised when a score exceeds it
+                        // by more than kTau (weights up to 2^kTau, which keeps
+                        // p * v_scale inside fp16 for every fp16 V): one vote.
+                        float mx0 = -INFINITY, mx1 = -INFINITY;
+    #pragma unroll
+                        for (int mi = 0; mi < MT; ++mi) {
+                            mx0 = fmaxf(mx0, fmaxf(sc[mi][0], sc[mi][2]));
+                            mx1 = fmaxf(mx1, fmaxf(sc[mi][1], sc[mi][3]));
+                        }
+                        if (__any_sync(kFull, mx0 > m_run[0] + M::kTau || mx1 > m_run[1] + M::kTau)) {
+                            mx0 = fmaxf(mx0, __shfl_xor_sync(kFull, mx0, 4));
+                            mx1 = fmaxf(mx1, __shfl_xor_sync(kFull, mx1, 4));
+                            mx0 = fmaxf(mx0, __shfl_xor_sync(kFull, mx0, 8));
+                            mx1 = fmaxf(mx1, __shfl_xor_sync(kFull, mx1, 8));
+                            mx0 = fmaxf(mx0, __shfl_xor_sync(kFull, mx0, 16));
+                            mx1 = fmaxf(mx1, __shfl_xor_sync(kFull, mx1, 16));
+                            const float mn0 = fmaxf(m_run[0], mx0), mn1 = fmaxf(m_run[1], mx1);
+                            const float a0 = mn0 == -INFINITY ? 1.f : fast_exp2(m_run[0] - mn0);
+                            const float a1 = mn1 == -INFINITY ? 1.f : fast_exp2(m_run[1] - mn1);
+                            m_run[0] = mn0;
+                            m_run[1] = mn1;
+                            l_run[0] *= a0, zv[0] *= a0, lf[0] *= a0;
+                            l_run[1] *= a1, zv[1] *= a1, lf[1] *= a1;
+    #pragma unroll
+                            for (int mt = 0; mt < 8; ++mt) {
+                                acc[mt][0] *= a0;
+                                acc[mt][1] *= a1;
+                                acc[mt][2] *= a0;
+                                acc[mt][3] *= a1;
                             }
                         }
-                        if constexpr (FMT == kF16)
-                            qk_mtile_f16(sb + (wt0 + 16 * mi + rg) * ROWB + M::KCB * r, Bh, df[mi]);
-                        else
-                            qk_mtile_int<FMT, L>(sb + (wt0 + 16 * mi + rg) * ROWB + M::KCB * r, Bq, d[mi]);
-                        zc[mi][0] = zk[0], zc[mi][1] = zk[1];
-                        dqc[mi][0] = dk[0], dqc[mi][1] = dk[1];
+                        const float mu0 = m_run[0] == -INFINITY ? 0.f : m_run[0];
+                        const float mu1 = m_run[1] == -INFINITY ? 0.f : m_run[1];
+                        uint32_t bf[MT][2];
+    #pragma unroll
+                        for (int mi = 0; mi < MT; ++mi) {
+                            const int row = wt0 + 16 * mi + rg;
+                            const bool ok0 = FULL || 16 * mi + rg < nval, ok1 = FULL || 16 * mi + rg + 8 < nval;
+                            const float p0 = fast_exp2(sc[mi][0] - mu0), p1 = fast_exp2(sc[mi][1] - mu1);
+                            const float p2 = fast_exp2(sc[mi][2] - mu0), p3 = fast_exp2(sc[mi][3] - mu1);
+                            l_run[0] += p0 + p2;
+                            l_run[1] += p1 + p3;
+                            float v0 = 1.f, v1 = 1.f;  // fp16 V: p is fed as is (0 on masked rows)
+                            if constexpr (FMT != kF16) {
+                                const __half* svs = reinterpret_cast<const __half*>(sb + p.off_vs);
+                                v0 = ok0 ? __half2float(svs[row]) : 0.f;
+                                v1 = ok1 ? __half2float(svs[row + 8]) : 0.f;
+                            }
+                            if (F::ZV) {
+                                const __half* svz = reinterpret_cast<const __half*>(sb + p.off_vz);
+                                const float z0 = ok0 ? __half2float(svz[row]) : 0.f;
+                                const float z1 = ok1 ? __half2float(svz[row + 8]) : 0.f;
+                                zv[0] = fmaf(p0, z0, fmaf(p2, z1, zv[0]));
+                                zv[1] = fmaf(p1, z0, fmaf(p3, z1, zv[1]));
+                            }
+                            const uint32_t pr0 = pack_h2(p0 * v0, p1 * v0);
+                            const uint32_t pr1 = pack_h2(p2 * v1, p3 * v1);
+                            if (!F::ZV && FMT != kF16) {
+                                // the exact sum of the fed weights cancels the V code offset
+                                fma_h2_2acc(pr0, 0x3c003c00u, lf[0], lf[1]);
+                                fma_h2_2acc(pr1, 0x3c003c00u, lf[0], lf[1]);
+                            }
+                            bf[mi][0] = movmatrix_trans(pr0);
+                            bf[mi][1] = movmatrix_trans(pr1);
+                        }
+                        // ---------------- PV (tensor pipe) ----------------
+    #pragma unroll
+                        for (int mi = 0; mi < MT; ++mi)
+                            if (FULL || 16 * mi < nval)
+                                pv_kstep<FMT>(sb + p.off_v + (wt0 + 16 * mi + vr) * ROWB + M::VCB * g,
+                                              bf[mi][0], bf[mi][1], acc);
                     }
                 }
-            }
-            // every warp waits for the stage's V copies before releasing it, also
-            // when none of its positions is live
-            if (!aborted && (misc[0] || !mbar_wait_bounded(&fullv[st], ph))) fail();
-            if (nval > 0 && !aborted) {
-                {
-                    // ---------------- scores ----------------
-                    float sc[MT][4];
-#pragma unroll
-                    for (int mi = 0; mi < MT; ++mi) {
-                        const int row = wt0 + 16 * mi + rg;
-                        const bool ok0 = 16 * mi + rg < nval, ok1 = 16 * mi + rg + 8 < nval;
-                        float dv[4];
-#pragma unroll
-                        for (int c = 0; c < 4; ++c) {
-                            if constexpr (FMT == kF16)
-                                dv[c] = df[mi][c];
-                            else if constexpr (L == 2)
-                                dv[c] = static_cast<float>(d[mi][0][c] * 256 + d[mi][1][c]);
-                            else
-                                dv[c] = fmaf(static_cast<float>(d[mi][0][c] * 256 + d[mi][1][c]), 256.f,
-                                             static_cast<float>(d[mi][2][c]));
-                        }
-                        if constexpr (FMT == kF16) {
-#pragma unroll
-                            for (int c = 0; c < 4; ++c) sc[mi][c] = dv[c] * p.qscale;
-                        } else if constexpr (FMT == kI8) {
-                            const __half* sks = reinterpret_cast<const __half*>(sb + p.off_ks);
-                            const float k0 = __half2float(sks[row]), k1 = __half2float(sks[row + 8]);
-                            sc[mi][0] = dv[0] * dqc[mi][0] * k0;
-                            sc[mi][1] = dv[1] * dqc[mi][1] * k0;
-                            sc[mi][2] = dv[2] * dqc[mi][0] * k1;
-                            sc[mi][3] = dv[3] * dqc[mi][1] * k1;
-                        } else {
-                            sc[mi][0] = fmaf(dv[0], dqc[mi][0], zc[mi][0]);
-                            sc[mi][1] = fmaf(dv[1], dqc[mi][1], zc[mi][1]);
-                            sc[mi][2] = fmaf(dv[2], dqc[mi][0], zc[mi][0]);
-                            sc[mi][3] = fmaf(dv[3], dqc[mi][1], zc[mi][1]);
-                        }
-                        // rows past the live length (and m-tiles past it) are masked
-                        if (!ok0) sc[mi][0] = sc[mi][1] = -INFINITY;
-                        if (!ok1) sc[mi][2] = sc[mi][3] = -INFINITY;
-                    }
-                    // ---------------- online softmax (log2 domain) ----------------
-                    // The running maximum is only raised when a score exceeds it
-                    // by more than kTau (weights up to 2^kTau, which keeps
-                    // p * v_scale inside fp16 for every fp16 V): one vote.
-                    float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-                    for (int mi = 0; mi < MT; ++mi) {
-                        mx0 = fmaxf(mx0, fmaxf(sc[mi][0], sc[mi][2]));
-                        mx1 = fmaxf(mx1, fmaxf(sc[mi][1], sc[mi][3]));
-                    }
-                    if (__any_sync(kFull, mx0 > m_run[0] + M::kTau || mx1 > m_run[1] + M::kTau)) {
-                        mx0 = fmaxf(mx0, __shfl_xor_sync(kFull, mx0, 4));
-                        mx1 = fmaxf(mx1, __shfl_xor_sync(kFull, mx1, 4));
-                        mx0 = fmaxf(mx0, __shfl_xor_sync(kFull, mx0, 8));
-                        mx1 = fmaxf(mx1, __shfl_xor_sync(kFull, mx1, 8));
-                        mx0 = fmaxf(mx0, __shfl_xor_sync(kFull, mx0, 16));
-                        mx1 = fmaxf(mx1, __shfl_xor_sync(kFull, mx1, 16));
-                        const float mn0 = fmaxf(m_run[0], mx0), mn1 = fmaxf(m_run[1], mx1);
-                        const float a0 = mn0 == -INFINITY ? 1.f : fast_exp2(m_run[0] - mn0);
-                        const float a1 = mn1 == -INFINITY ? 1.f : fast_exp2(m_run[1] - mn1);
-                        m_run[0] = mn0;
-                        m_run[1] = mn1;
-                        l_run[0] *= a0, zv[0] *= a0, lf[0] *= a0;
-                        l_run[1] *= a1, zv[1] *= a1, lf[1] *= a1;
-#pragma unroll
-                        for (int mt = 0; mt < 8; ++mt) {
-                            acc[mt][0] *= a0;
-                            acc[mt][1] *= a1;
-                            acc[mt][2] *= a0;
-                            acc[mt][3] *= a1;
-                        }
-                    }
-                    const float mu0 = m_run[0] == -INFINITY ? 0.f : m_run[0];
-                    const float mu1 = m_run[1] == -INFINITY ? 0.f : m_run[1];
-                    uint32_t bf[MT][2];
-#pragma unroll
-                    for (int mi = 0; mi < MT; ++mi) {
-                        const int row = wt0 + 16 * mi + rg;
-                        const bool ok0 = 16 * mi + rg < nval, ok1 = 16 * mi + rg + 8 < nval;
-                        const float p0 = fast_exp2(sc[mi][0] - mu0), p1 = fast_exp2(sc[mi][1] - mu1);
-                        const float p2 = fast_exp2(sc[mi][2] - mu0), p3 = fast_exp2(sc[mi][3] - mu1);
-                        l_run[0] += p0 + p2;
-                        l_run[1] += p1 + p3;
-                        float v0 = 1.f, v1 = 1.f;  // fp16 V: p is fed as is (0 on masked rows)
-                        if constexpr (FMT != kF16) {
-                            const __half* svs = reinterpret_cast<const __half*>(sb + p.off_vs);
-                            v0 = ok0 ? __half2float(svs[row]) : 0.f;
-                            v1 = ok1 ? __half2float(svs[row + 8]) : 0.f;
-                        }
-                        if (F::ZV) {
-                            const __half* svz = reinterpret_cast<const __half*>(sb + p.off_vz);
-                            const float z0 = ok0 ? __half2float(svz[row]) : 0.f;
-                            const float z1 = ok1 ? __half2float(svz[row + 8]) : 0.f;
-                            zv[0] = fmaf(p0, z0, fmaf(p2, z1, zv[0]));
-                            zv[1] = fmaf(p1, z0, fmaf(p3, z1, zv[1]));
-                        }
-                        const uint32_t pr0 = pack_h2(p0 * v0, p1 * v0);
-                        const uint32_t pr1 = pack_h2(p2 * v1, p3 * v1);
-                        if (!F::ZV && FMT != kF16) {
-                            // the exact sum of the fed weights cancels the V code offset
-                            fma_h2_2acc(pr0, 0x3c003c00u, lf[0], lf[1]);
-                            fma_h2_2acc(pr1, 0x3c003c00u, lf[0], lf[1]);
-                        }
-                        bf[mi][0] = movmatrix_trans(pr0);
-                        bf[mi][1] = movmatrix_trans(pr1);
-                    }
-                    // ---------------- PV (tensor pipe) ----------------
-#pragma unroll
-                    for (int mi = 0; mi < MT; ++mi)
-                        if (16 * mi < nval)
-                            pv_kstep<FMT>(sb + p.off_v + (wt0 + 16 * mi + vr) * ROWB + M::VCB * g,
-                                          bf[mi][0], bf[mi][1], acc);
-                }
-            }
+            };
+            if (nval >= TW)
+                tile_body(std::true_type{});
+            else
+                tile_body(std::false_type{});
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[st]);
 
