@@ -79,7 +79,7 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--profile", action="store_true",
                     help="profiler-friendly run: one warm replay, short e2e legs (timings not for reporting)")
-    ap.add_argument("--case", choices=["f16", "int8", "int4", "int4_asym"],
+    ap.add_argument("--case", choices=["f16", "int8", "int4", "int4_asym"] + list(QUANT_CASES),
                     help="profiling case: only `--launches` decode launches of this KV format at the config-1 "
                          "shape (one copy of the inputs, larger than L2), no timing, no JSON line")
     ap.add_argument("--launches", type=int, default=3, help="launches of --case")
@@ -672,14 +672,35 @@ def run_ours(args):
     return 0
 
 
+# the KV quantize / pack and materialize ops, for ncu captures of one kernel
+QUANT_CASES = {
+    "q_int8": lambda L, x, i8, i4: L.quantize_per_token(x),
+    "q_k4": lambda L, x, i8, i4: L.quantize_k_per_channel_groupwise_int4(x, GS),
+    "q_v4": lambda L, x, i8, i4: L.quantize_v_per_token_int4(x),
+    "q_k4a": lambda L, x, i8, i4: L.quantize_k_per_channel_groupwise_int4_asym(x, GS),
+    "q_v4a": lambda L, x, i8, i4: L.quantize_v_per_token_int4_asym(x),
+    "dq_int8": lambda L, x, i8, i4: L.dequantize_int8(i8[0], i8[1], i8[0], i8[1]),
+    "dq_int4a": lambda L, x, i8, i4: L.dequantize_int4(i4[0], i4[1], i4[3], i4[4], GS, -1, i4[2], i4[5]),
+}
+
+
 def run_case(args):
-    """A few decode launches of one KV format for ncu captures (small, bounded)."""
+    """A few launches of one decode format or one KV quantize / materialize
+    op at [batch, 8, seqlen, 128], for ncu captures (small, bounded)."""
     import torch
     import llmik_cuda as L
     dev = torch.device("cuda", 0)
-    wl = Workload(torch, L, dev, args.case, args.batch, args.seqlen, 0, 1)
-    for i in range(args.launches):
-        wl.step(i)
+    if args.case in QUANT_CASES:
+        g = torch.Generator(device=dev).manual_seed(11)
+        x = torch.randn(args.batch, HKV, args.seqlen, D, generator=g, device=dev).half()
+        i8 = L.quantize_per_token(x)
+        i4 = L.quantize_k_per_channel_groupwise_int4_asym(x, GS) + L.quantize_v_per_token_int4_asym(x)
+        for i in range(args.launches):
+            QUANT_CASES[args.case](L, x, i8, i4)
+    else:
+        wl = Workload(torch, L, dev, args.case, args.batch, args.seqlen, 0, 1)
+        for i in range(args.launches):
+            wl.step(i)
     torch.cuda.synchronize()
     print(f"case {args.case}: {args.launches} launches ok", flush=True)
     return 0

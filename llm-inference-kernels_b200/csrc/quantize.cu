@@ -33,13 +33,14 @@ constexpr float kAsymScaleFloor = 5.9604644775390625e-8f;  // 2^-24, smallest fp
 // nearest), as the oracle computes them, without a division in the common
 // case. With r = RN(1/s), y = RN(x * r) lies within 2^-22.4 |x / s| of that
 // quotient, i.e. within 2.3e-5 for the |x / s| <= 128 these kernels produce;
-// so y rounds to the quotient's nearest integer unless it lies within 1e-4 of
+// so y rounds to the quotient's nearest integer unless it lies within 4e-5 of
 // a half-integer, and only those elements (and non-finite ones) take the
 // exact division. Rounding adds 1.5 * 2^23 (fp32 addition rounds half to
 // even, like rintf): for |v| < 2^22 the sum holds the integer in its low
 // mantissa bits, from which the codes are packed without a float-to-int
 // conversion.
 constexpr float kRoundMagic = 12582912.0f;  // 1.5 * 2^23
+constexpr float kNearTie = 0.49996f;        // |y - rint(y)| at or above this: exact division
 
 // bytes 0..3 = low bytes of a, b, c, d
 __device__ __forceinline__ uint32_t pack_bytes4(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
@@ -136,7 +137,7 @@ __device__ __forceinline__ void quant_row(const Raw16& raw, long long drow, uint
     for (int i = 0; i < CH; ++i) {
         const float y = __fmul_rn(xv[i], rf);
         float tt = __fadd_rn(y, kRoundMagic);
-        exact |= !(fabsf(__fsub_rn(y, __fsub_rn(tt, kRoundMagic))) < 0.4999f);
+        exact |= !(fabsf(__fsub_rn(y, __fsub_rn(tt, kRoundMagic))) < kNearTie);
         if (MODE == kTokI4Asym) tt = fminf(fmaxf(tt, kRoundMagic), kRoundMagic + 15.0f);
         tv[i] = tt;
     }
@@ -195,6 +196,154 @@ __global__ void __launch_bounds__(256, 4) quant_token_kernel(const __half* __res
             ++slab;
         }
         quant_row<MODE>(raw[k], drow, codes, scale, zero, l, mask);
+    }
+}
+
+// ---- per-token quantize of a whole tensor: 4 lanes per row -----------------
+// Each row is held by 4 lanes (32 channels, 64 bytes each), so the per-row
+// work (statistics, scale, reciprocal) is shared by 128 elements per lane
+// quartet; the grid is persistent and every lane quartet prefetches its next
+// row while it quantizes the current one. Same arithmetic as quant_row.
+
+// Division of 32-bit row indices by a launch constant with one multiply-high
+// (the round-up method of Granlund and Montgomery): q = (umulhi(x, m) + x) >> s.
+struct RowDiv {
+    uint32_t d, m, s;
+    __device__ __forceinline__ uint32_t q(uint32_t x) const { return (__umulhi(x, m) + x) >> s; }
+};
+RowDiv make_rowdiv(uint32_t d) {
+    RowDiv f{d, 0u, 0u};
+    while ((uint64_t{1} << f.s) < d) ++f.s;
+    f.m = static_cast<uint32_t>(((uint64_t{1} << 32) * ((uint64_t{1} << f.s) - d)) / d + 1);
+    return f;
+}
+
+struct Raw32 {
+    uint4 v[4];
+};
+
+// bytes b0..b3 of the result = (c[2i] & 0xF) | (c[2i+1] & 0xF) << 4
+__device__ __forceinline__ uint32_t pack_nibbles8(const uint32_t* c) {
+    uint32_t b[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) b[i] = (c[2 * i] & 0xFu) | ((c[2 * i + 1] << 4) & 0xF0u);
+    return pack_bytes4(b[0], b[1], b[2], b[3]);
+}
+
+template <int MODE>
+__device__ __forceinline__ void quant_row32(const Raw32& raw, long long drow, uint8_t* __restrict__ codes,
+                                            __half* __restrict__ scale, __half* __restrict__ zero, int l,
+                                            unsigned mask) {
+    const __half2* h = reinterpret_cast<const __half2*>(raw.v);  // 16 pairs
+    float sf, zf = 0.f;
+    if (MODE == kTokI4Asym) {
+        __half2 mn2 = h[0], mx2 = h[0];
+#pragma unroll
+        for (int i = 1; i < 16; ++i) {
+            mn2 = __hmin2(mn2, h[i]);
+            mx2 = __hmax2(mx2, h[i]);
+        }
+        float mn = fminf(__low2float(mn2), __high2float(mn2));
+        float mx = fmaxf(__low2float(mx2), __high2float(mx2));
+#pragma unroll
+        for (int m = 1; m < 4; m <<= 1) {
+            mn = fminf(mn, __shfl_xor_sync(mask, mn, m));
+            mx = fmaxf(mx, __shfl_xor_sync(mask, mx, m));
+        }
+        const float sc = fmaxf(__fdiv_rn(__fsub_rn(mx, mn), 15.0f), kAsymScaleFloor);
+        const __half sh = __float2half_rn(sc);
+        const __half zh = __float2half_rn(mn);
+        sf = __half2float(sh);
+        zf = __half2float(zh);
+        if (l == 0) {
+            scale[drow] = sh;
+            zero[drow] = zh;
+        }
+    } else {
+        constexpr float qmax = (MODE == kTokI8) ? 127.0f : 7.0f;
+        __half2 am2 = __habs2(h[0]);
+#pragma unroll
+        for (int i = 1; i < 16; ++i) am2 = __hmax2(am2, __habs2(h[i]));
+        float amax = fmaxf(__low2float(am2), __high2float(am2));
+#pragma unroll
+        for (int m = 1; m < 4; m <<= 1) amax = fmaxf(amax, __shfl_xor_sync(mask, amax, m));
+        sf = fmaxf(__fdiv_rn(amax, qmax), 1e-8f);
+        if (l == 0) scale[drow] = __float2half_rn(sf);
+    }
+    const float rf = __frcp_rn(sf);
+    constexpr float lo = MODE == kTokI4Asym ? 0.0f : (MODE == kTokI8 ? -127.0f : -7.0f);
+    constexpr float hi = MODE == kTokI4Asym ? 15.0f : (MODE == kTokI8 ? 127.0f : 7.0f);
+#pragma unroll
+    for (int ck = 0; ck < 2; ++ck) {  // 16 channels at a time
+        float xv[16], tv[16];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float2 u = __half22float2(h[8 * ck + i]);
+            xv[2 * i] = MODE == kTokI4Asym ? __fsub_rn(u.x, zf) : u.x;
+            xv[2 * i + 1] = MODE == kTokI4Asym ? __fsub_rn(u.y, zf) : u.y;
+        }
+        bool exact = false;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const float y = __fmul_rn(xv[i], rf);
+            float tt = __fadd_rn(y, kRoundMagic);
+            exact |= !(fabsf(__fsub_rn(y, __fsub_rn(tt, kRoundMagic))) < kNearTie);
+            if (MODE == kTokI4Asym) tt = fminf(fmaxf(tt, kRoundMagic), kRoundMagic + 15.0f);
+            tv[i] = tt;
+        }
+        if (exact) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+                tv[i] = __fadd_rn(fminf(fmaxf(rintf(__fdiv_rn(xv[i], sf)), lo), hi), kRoundMagic);
+        }
+        uint32_t c[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) c[i] = static_cast<uint32_t>(__float_as_int(tv[i]));
+        if (MODE == kTokI8) {
+            reinterpret_cast<uint4*>(codes + drow * kHeadDim + l * 32)[ck] =
+                make_uint4(pack_bytes4(c[0], c[1], c[2], c[3]), pack_bytes4(c[4], c[5], c[6], c[7]),
+                           pack_bytes4(c[8], c[9], c[10], c[11]), pack_bytes4(c[12], c[13], c[14], c[15]));
+        } else {
+            reinterpret_cast<uint2*>(codes + drow * (kHeadDim / 2) + l * 16)[ck] =
+                make_uint2(pack_nibbles8(c), pack_nibbles8(c + 8));
+        }
+    }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(256, 3) quant_rows_kernel(const __half* __restrict__ x, uint8_t* __restrict__ codes,
+                                                         __half* __restrict__ scale, __half* __restrict__ zero,
+                                                         uint32_t n_rows, RowDiv per_slab, long long dst_pos,
+                                                         long long dst_buf) {
+    const int l = threadIdx.x & 3;
+    const unsigned mask = 0xFu << (threadIdx.x & 28);
+    const uint32_t stride = (gridDim.x * blockDim.x) >> 2;
+    uint32_t row = (blockIdx.x * blockDim.x + threadIdx.x) >> 2;
+    if (row >= n_rows) return;  // whole lane quartets leave together
+    auto load = [&](uint32_t rw) {
+        Raw32 r;
+        const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<long long>(rw) * kHeadDim + l * 32);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) r.v[j] = __ldcs(src + j);
+        return r;
+    };
+    auto quant = [&](const Raw32& r, uint32_t rw) {
+        const uint32_t slab = per_slab.q(rw);
+        const long long t = rw - slab * per_slab.d;
+        quant_row32<MODE>(r, static_cast<long long>(slab) * dst_buf + dst_pos + t, codes, scale, zero, l, mask);
+    };
+    // two rows in flight, in alternating register sets
+    Raw32 a = load(row), b = a;
+    while (true) {
+        const uint32_t r1 = row + stride;
+        if (r1 < n_rows) b = load(r1);
+        quant(a, row);
+        if (r1 >= n_rows) break;
+        const uint32_t r2 = r1 + stride;
+        if (r2 < n_rows) a = load(r2);
+        quant(b, r1);
+        if (r2 >= n_rows) break;
+        row = r2;
     }
 }
 
@@ -259,7 +408,7 @@ __device__ __forceinline__ uint32_t quant8_k(const uint4& raw, const float (&sc)
     for (int i = 0; i < 8; ++i) {
         const float y = __fmul_rn(xv[i], rc[i]);
         float tt = __fadd_rn(y, kRoundMagic);
-        exact |= !(fabsf(__fsub_rn(y, __fsub_rn(tt, kRoundMagic))) < 0.4999f);
+        exact |= !(fabsf(__fsub_rn(y, __fsub_rn(tt, kRoundMagic))) < kNearTie);
         // asymmetric codes need the clamp (the zero point is rounded to fp16);
         // symmetric ones cannot leave [-7, 7]: |x| <= absmax <= 7 s (1 + 2^-24)
         if (ASYM) tt = fminf(fmaxf(tt, kRoundMagic), kRoundMagic + 15.0f);
@@ -414,7 +563,18 @@ lik_status launch_quant_token(int mode, const void* x, void* codes, void* scale,
     uint8_t* c = static_cast<uint8_t*>(codes);
     __half* s = static_cast<__half*>(scale);
     __half* z = static_cast<__half*>(zero);
-    switch (mode) {
+    DeviceInfo di;
+    if (n_rows < (1LL << 31) && n_tokens > 0 && device_info(di, err)) {
+        const long long need = (n_rows + 63) / 64;  // 64 rows per 256-thread block
+        const unsigned nb = static_cast<unsigned>(std::min<long long>(need, 3LL * di.sm_count));
+        const RowDiv per_slab = make_rowdiv(static_cast<uint32_t>(n_tokens));
+        const uint32_t nr = static_cast<uint32_t>(n_rows);
+        switch (mode) {
+            case kTokI8: quant_rows_kernel<kTokI8><<<nb, 256, 0, stream>>>(xh, c, s, z, nr, per_slab, dst_pos, dst_buf_len); break;
+            case kTokI4Sym: quant_rows_kernel<kTokI4Sym><<<nb, 256, 0, stream>>>(xh, c, s, z, nr, per_slab, dst_pos, dst_buf_len); break;
+            default: quant_rows_kernel<kTokI4Asym><<<nb, 256, 0, stream>>>(xh, c, s, z, nr, per_slab, dst_pos, dst_buf_len); break;
+        }
+    } else switch (mode) {
         case kTokI8:
             quant_token_kernel<kTokI8><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(xh, c, s, z, n_rows, n_tokens,
                                                                                          dst_pos, dst_buf_len);
