@@ -823,10 +823,17 @@ __device__ __forceinline__ void pv_kstep(const uint8_t* vrow, uint32_t b0, uint3
 // limbs laid out as QK B fragments, plus the head's score constant (asym:
 // sum_c q_c z_c; sym: -8 * the fed weights' sum, cancelling the +8 code
 // offset) and step.
+// INT4 tensor pipe with four heads per unit: the consumer warps form two
+// groups of four that take alternate tiles (64 positions per warp and tile,
+// run as two 32-position halves), so that one group's weight preparation and
+// barrier overlap the other group's tensor-pipe work.
+template <int FMT, int HB, bool MMA>
+constexpr bool kSplitGroups = MMA && Fmt<FMT>::KG && HB == 4;
+
 template <int FMT, int HB>
 __device__ __forceinline__ void prep_int4_weights(const DecodeParams& p, const uint8_t* sb, long long t0, int ntok,
-                                                  int w, int lane, int pcb, int phf, int head, const float (&qh)[4],
-                                                  long long unit) {
+                                                  int gi0, int gstep, int lane, int pcb, int phf, int head,
+                                                  const float (&qh)[4], long long unit) {
     using F = Fmt<FMT>;
     constexpr int L = MmaFmt<FMT>::L;
     constexpr float kFix = 8388607.f;  // 2^23 - 1
@@ -836,9 +843,9 @@ __device__ __forceinline__ void prep_int4_weights(const DecodeParams& p, const u
     float* zk = reinterpret_cast<float*>(const_cast<uint8_t*>(sb) + p.off_zk);
     float* dq = zk + p.ngw * HB;
     const int r = lane >> 3, ks = (lane >> 1) & 3;
-    // slices gi * HB + head; warp w takes the ones congruent to w mod 8
+    // slices gi * HB + head for gi = gi0, gi0 + gstep, ...
 #pragma unroll 1
-    for (int gi = w / HB; gi < ngrp; gi += kNCW / HB) {
+    for (int gi = gi0; gi < ngrp; gi += gstep) {
         const __half* gsp;
         const __half* gzp = nullptr;
         if (p.kg_smem) {
@@ -935,7 +942,7 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
         for (int s = 0; s < p.nst; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&fullv[s], 1);
-            mbar_init(&empty[s], kNCW);
+            mbar_init(&empty[s], kSplitGroups<FMT, HB, MMA> ? kNCW / 2 : kNCW);
         }
         mbar_init(epi_full, kNCW);
         mbar_init(epi_empty, 1);
@@ -1032,7 +1039,9 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                     *reinterpret_cast<uint4*>(sb + p.off_v + ntok * ROWB + idx * 16) = make_uint4(0u, 0u, 0u, 0u);
                 __syncwarp();
             }
-            const bool new_unit = (j == 0 || ti == 0);
+            // q rides with a unit's first tile in this CTA (and, when the
+            // consumer warp groups alternate tiles, with its second as well)
+            const bool new_unit = (j == 0 || ti == 0) || (kSplitGroups<FMT, HB, MMA> && (j == 1 || ti == 1));
             if (lane == 0 && p.paged) {
                 // gather the tile block by block (one bulk copy per block touched)
                 const int bs = p.block_size;
@@ -1198,7 +1207,11 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
         // (INT4 odd channels were fed as 16 n), 1 for fp16 V
         constexpr float kSub = FMT == kF16 ? 1.f : 16777216.f;
         constexpr float kScHi = M::I4 ? kSub / 16.f : kSub;
-        const int wt0 = w * TW;
+        constexpr bool SPLIT = kSplitGroups<FMT, HB, MMA>;
+        constexpr int NHALF = SPLIT ? 2 : 1;  // TW-position halves of a warp's share per tile
+        const int wg = SPLIT ? (w & 3) : w;    // warp within its group
+        const int wgrp = SPLIT ? (w >> 2) : 0;
+        const int wt0 = wg * NHALF * TW;
         // INT4: a warp's TW positions of a tile lie in one K group
         const bool one_group = F::KG && p.group_size % TW == 0;
         const long long first_unit_of_cta = p.fd_tpu.q(tb);
@@ -1240,8 +1253,9 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
         // pcb + phf + 2 i)
         const int phf = lane & 1;
         const int pcb = 32 * (lane >> 3) + 8 * ((lane >> 1) & 3);
-        const int ph_head = w % HB;
+        const int ph_head = SPLIT ? wg : w % HB;
         float qh[4] = {0.f, 0.f, 0.f, 0.f};
+        long long q_unit = -1;  // unit whose q is in qh
 
         int st = 0;
         uint32_t ph = 0;
@@ -1256,6 +1270,9 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                     seq_len = cl < 0 ? 0 : (cl > p.seqlen ? p.seqlen : cl);
                 }
             }
+            // tiles alternate between the two warp groups (SPLIT); the stage and
+            // segment bookkeeping below runs for every tile
+            if (!SPLIT || (((i - tb) & 1) == wgrp)) {
             if (!aborted && !stage_wait(&full[st], ph, misc)) fail();
             const uint8_t* sb = smem + static_cast<size_t>(st) * p.stage_bytes;
             const long long t0 = ti * T;
@@ -1313,8 +1330,10 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                 }
             }
             if constexpr (F::KG) {
-                if (new_unit) {
+                if (unit != q_unit) {
+                    q_unit = unit;
                     // q of this warp's head arrived with the unit's first stage
+                    // (of this warp group)
                     const uint4 u = *reinterpret_cast<const uint4*>(
                         reinterpret_cast<const __half*>(sb + p.off_q) + ph_head * kHeadDim + pcb);
                     const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
@@ -1322,11 +1341,13 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                     for (int i2 = 0; i2 < 4; ++i2) qh[i2] = half_of(uw[i2], phf) * p.qscale;
                 }
                 if (!aborted && ntok > 0)
-                    prep_int4_weights<FMT, HB>(p, sb, t0, ntok, w, lane, pcb, phf, ph_head, qh, unit);
-                // every consumer warp passes here once per tile, aborted or not
-                named_bar_sync(2, kNCW * 32);
+                    prep_int4_weights<FMT, HB>(p, sb, t0, ntok, SPLIT ? 0 : w / HB, SPLIT ? 1 : kNCW / HB, lane,
+                                               pcb, phf, ph_head, qh, unit);
+                // every consumer warp of the tile passes here once, aborted or not
+                named_bar_sync(2 + wgrp, (SPLIT ? kNCW / 2 : kNCW) * 32);
             }
-            const int nval = aborted ? 0 : ntok - wt0;
+            int wt = wt0;  // first position of the half in progress
+            int nval = 0;
             // The common case, every position of the warp's share live, runs a
             // copy of the tile body without the per-row masking.
             auto tile_body = [&](auto full_tag) {
@@ -1342,7 +1363,7 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                         if (FULL || 16 * mi < nval) {
                             if constexpr (F::KG) {
                               if (mi == 0 || !one_group) {
-                                const int gi = static_cast<int>(p.fd_gs.q(t0 + wt0 + 16 * mi) - p.fd_gs.q(t0));
+                                const int gi = static_cast<int>(p.fd_gs.q(t0 + wt + 16 * mi) - p.fd_gs.q(t0));
                                 if (gi != cur_gi) {
                                     cur_gi = gi;
                                     const uint4* bw = reinterpret_cast<const uint4*>(
@@ -1366,9 +1387,9 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                               }
                             }
                             if constexpr (FMT == kF16)
-                                qk_mtile_f16(sb + (wt0 + 16 * mi + rg) * ROWB + M::KCB * r, Bh, df[mi]);
+                                qk_mtile_f16(sb + (wt + 16 * mi + rg) * ROWB + M::KCB * r, Bh, df[mi]);
                             else
-                                qk_mtile_int<FMT, L>(sb + (wt0 + 16 * mi + rg) * ROWB + M::KCB * r, Bq, d[mi]);
+                                qk_mtile_int<FMT, L>(sb + (wt + 16 * mi + rg) * ROWB + M::KCB * r, Bq, d[mi]);
                             zc[mi][0] = zk[0], zc[mi][1] = zk[1];
                             dqc[mi][0] = dk[0], dqc[mi][1] = dk[1];
                         }
@@ -1383,7 +1404,7 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                         float sc[MT][4];
     #pragma unroll
                         for (int mi = 0; mi < MT; ++mi) {
-                            const int row = wt0 + 16 * mi + rg;
+                            const int row = wt + 16 * mi + rg;
                             const bool ok0 = FULL || 16 * mi + rg < nval, ok1 = FULL || 16 * mi + rg + 8 < nval;
                             float dv[4];
     #pragma unroll
@@ -1453,7 +1474,7 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                         uint32_t bf[MT][2];
     #pragma unroll
                         for (int mi = 0; mi < MT; ++mi) {
-                            const int row = wt0 + 16 * mi + rg;
+                            const int row = wt + 16 * mi + rg;
                             const bool ok0 = FULL || 16 * mi + rg < nval, ok1 = FULL || 16 * mi + rg + 8 < nval;
                             const float p0 = fast_exp2(sc[mi][0] - mu0), p1 = fast_exp2(sc[mi][1] - mu1);
                             const float p2 = fast_exp2(sc[mi][2] - mu0), p3 = fast_exp2(sc[mi][3] - mu1);
@@ -1486,17 +1507,23 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
     #pragma unroll
                         for (int mi = 0; mi < MT; ++mi)
                             if (FULL || 16 * mi < nval)
-                                pv_kstep<FMT>(sb + p.off_v + (wt0 + 16 * mi + vr) * ROWB + M::VCB * g,
+                                pv_kstep<FMT>(sb + p.off_v + (wt + 16 * mi + vr) * ROWB + M::VCB * g,
                                               bf[mi][0], bf[mi][1], acc);
                     }
                 }
             };
-            if (nval >= TW)
-                tile_body(std::true_type{});
-            else
-                tile_body(std::false_type{});
+#pragma unroll 1
+            for (int hf = 0; hf < NHALF; ++hf) {
+                wt = wt0 + hf * TW;
+                nval = aborted ? 0 : ntok - wt;
+                if (nval >= TW)
+                    tile_body(std::true_type{});
+                else
+                    tile_body(std::false_type{});
+            }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[st]);
+            }  // tile of this warp group
 
             // ---------------- end of a unit segment ----------------
             if (ti == p.tpu - 1 || i == te - 1) {
