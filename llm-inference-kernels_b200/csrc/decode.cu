@@ -823,12 +823,15 @@ __device__ __forceinline__ void pv_kstep(const uint8_t* vrow, uint32_t b0, uint3
 // limbs laid out as QK B fragments, plus the head's score constant (asym:
 // sum_c q_c z_c; sym: -8 * the fed weights' sum, cancelling the +8 code
 // offset) and step.
-// INT4 tensor pipe with four heads per unit: the consumer warps form two
-// groups of four that take alternate tiles (64 positions per warp and tile,
-// run as two 32-position halves), so that one group's weight preparation and
-// barrier overlap the other group's tensor-pipe work.
+// INT4 tensor pipe with four heads per unit: the consumer warps form
+// kWarpGroups groups that take tiles in turn (each warp covering
+// kWarpGroups x 32 positions of its group's tiles, 32 at a time), so that one
+// group's weight preparation and barrier overlap the other groups'
+// tensor-pipe work (measured: two groups -10% on a config-4-sized INT4
+// launch; four groups -2% more there but +1.2 us at config 1). 1: all
+// consumer warps share every tile.
 template <int FMT, int HB, bool MMA>
-constexpr bool kSplitGroups = MMA && Fmt<FMT>::KG && HB == 4;
+constexpr int kWarpGroups = (MMA && Fmt<FMT>::KG && HB == 4) ? 2 : 1;
 
 template <int FMT, int HB>
 __device__ __forceinline__ void prep_int4_weights(const DecodeParams& p, const uint8_t* sb, long long t0, int ntok,
@@ -942,7 +945,7 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
         for (int s = 0; s < p.nst; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&fullv[s], 1);
-            mbar_init(&empty[s], kSplitGroups<FMT, HB, MMA> ? kNCW / 2 : kNCW);
+            mbar_init(&empty[s], kNCW / kWarpGroups<FMT, HB, MMA>);
         }
         mbar_init(epi_full, kNCW);
         mbar_init(epi_empty, 1);
@@ -1039,9 +1042,9 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                     *reinterpret_cast<uint4*>(sb + p.off_v + ntok * ROWB + idx * 16) = make_uint4(0u, 0u, 0u, 0u);
                 __syncwarp();
             }
-            // q rides with a unit's first tile in this CTA (and, when the
-            // consumer warp groups alternate tiles, with its second as well)
-            const bool new_unit = (j == 0 || ti == 0) || (kSplitGroups<FMT, HB, MMA> && (j == 1 || ti == 1));
+            // q rides with a unit's first tile in this CTA (with its first
+            // kWarpGroups tiles when consumer warp groups take tiles in turn)
+            const bool new_unit = j < kWarpGroups<FMT, HB, MMA> || ti < kWarpGroups<FMT, HB, MMA>;
             if (lane == 0 && p.paged) {
                 // gather the tile block by block (one bulk copy per block touched)
                 const int bs = p.block_size;
@@ -1207,10 +1210,13 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
         // (INT4 odd channels were fed as 16 n), 1 for fp16 V
         constexpr float kSub = FMT == kF16 ? 1.f : 16777216.f;
         constexpr float kScHi = M::I4 ? kSub / 16.f : kSub;
-        constexpr bool SPLIT = kSplitGroups<FMT, HB, MMA>;
-        constexpr int NHALF = SPLIT ? 2 : 1;  // TW-position halves of a warp's share per tile
-        const int wg = SPLIT ? (w & 3) : w;    // warp within its group
-        const int wgrp = SPLIT ? (w >> 2) : 0;
+        constexpr int NG = kWarpGroups<FMT, HB, MMA>;
+        constexpr bool SPLIT = NG > 1;
+        constexpr int GW = kNCW / NG;       // warps per group
+        constexpr int NHALF = NG;           // TW-position parts of a warp's share per tile
+        constexpr int HPW = SPLIT ? HB / GW : 1;  // INT4: heads whose weights a warp prepares
+        const int wg = w % GW;              // warp within its group
+        const int wgrp = w / GW;
         const int wt0 = wg * NHALF * TW;
         // INT4: a warp's TW positions of a tile lie in one K group
         const bool one_group = F::KG && p.group_size % TW == 0;
@@ -1253,8 +1259,8 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
         // pcb + phf + 2 i)
         const int phf = lane & 1;
         const int pcb = 32 * (lane >> 3) + 8 * ((lane >> 1) & 3);
-        const int ph_head = SPLIT ? wg : w % HB;
-        float qh[4] = {0.f, 0.f, 0.f, 0.f};
+        const int ph_head = SPLIT ? wg * HPW : w % HB;  // first of the warp's HPW heads
+        float qh[HPW][4] = {};
         long long q_unit = -1;  // unit whose q is in qh
 
         int st = 0;
@@ -1272,7 +1278,7 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
             }
             // tiles alternate between the two warp groups (SPLIT); the stage and
             // segment bookkeeping below runs for every tile
-            if (!SPLIT || (((i - tb) & 1) == wgrp)) {
+            if (!SPLIT || (((i - tb) % NG) == wgrp)) {
             if (!aborted && !stage_wait(&full[st], ph, misc)) fail();
             const uint8_t* sb = smem + static_cast<size_t>(st) * p.stage_bytes;
             const long long t0 = ti * T;
@@ -1334,17 +1340,23 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                     q_unit = unit;
                     // q of this warp's head arrived with the unit's first stage
                     // (of this warp group)
-                    const uint4 u = *reinterpret_cast<const uint4*>(
-                        reinterpret_cast<const __half*>(sb + p.off_q) + ph_head * kHeadDim + pcb);
-                    const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-                    for (int i2 = 0; i2 < 4; ++i2) qh[i2] = half_of(uw[i2], phf) * p.qscale;
+                    for (int hh = 0; hh < HPW; ++hh) {
+                        const uint4 u = *reinterpret_cast<const uint4*>(
+                            reinterpret_cast<const __half*>(sb + p.off_q) + (ph_head + hh) * kHeadDim + pcb);
+                        const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                        for (int i2 = 0; i2 < 4; ++i2) qh[hh][i2] = half_of(uw[i2], phf) * p.qscale;
+                    }
                 }
-                if (!aborted && ntok > 0)
-                    prep_int4_weights<FMT, HB>(p, sb, t0, ntok, SPLIT ? 0 : w / HB, SPLIT ? 1 : kNCW / HB, lane,
-                                               pcb, phf, ph_head, qh, unit);
+                if (!aborted && ntok > 0) {
+#pragma unroll
+                    for (int hh = 0; hh < HPW; ++hh)
+                        prep_int4_weights<FMT, HB>(p, sb, t0, ntok, SPLIT ? 0 : w / HB, SPLIT ? 1 : kNCW / HB,
+                                                   lane, pcb, phf, ph_head + hh, qh[hh], unit);
+                }
                 // every consumer warp of the tile passes here once, aborted or not
-                named_bar_sync(2 + wgrp, (SPLIT ? kNCW / 2 : kNCW) * 32);
+                named_bar_sync(2 + wgrp, GW * 32);
             }
             int wt = wt0;  // first position of the half in progress
             int nval = 0;
