@@ -7,7 +7,8 @@
 //           slab (HB = the GQA group, or a divisor of it), so every KV byte is
 //           read from HBM exactly once per step (the reference launches one
 //           CTA per query head and re-reads each slab G times, relying on L2).
-//   tile  = T consecutive KV positions of one unit (T * row bytes = 32 KB).
+//   tile  = T consecutive KV positions of one unit (fp16 128, INT8 / INT4
+//           256 positions: 32-64 KB of codes).
 //   The flattened (unit, tile) sequence is split evenly over a persistent grid
 //   of one CTA per SM: CTA c owns tiles [c*TT/C, (c+1)*TT/C). A CTA's range may
 //   cover whole units (written straight to `out`) and partial units at its
@@ -16,25 +17,31 @@
 //   them). No CTA ever waits for another CTA.
 //
 // Inside a CTA
-//   warp 8 (producer): one lane issues 1-D bulk async copies
-//     (cp.async.bulk, no tensor map, no multicast) of the K and V tile plus the
-//     per-token / per-group scales into an NST-deep shared-memory ring, each
-//     stage tracked by a "full" mbarrier with transaction bytes and an "empty"
-//     mbarrier the consumers arrive on.
-//   warps 0-7 (consumers): warp w owns positions [w*T/8, (w+1)*T/8) of every
-//     tile and keeps its own online-softmax state (m, l, acc) for all HB heads,
-//     so the tile loop has no CTA-wide barrier. Per warp and tile:
-//       QK : 8 lanes per position, 16 channels per lane. K codes are
-//            dequantized to fp16 exactly as the reference oracle does
-//            (fp16(code * scale [+ zero]); the INT8 token scale multiplies
-//            the reduced score instead), then multiplied with q in fp16 by
-//            sm_100's mixed-precision fma.rn.f32.f16 (exact product, fp32
-//            sum). Partial sums are reduce-scattered over the 8 lanes so each
-//            lane ends with one head's score.
-//       softmax: scores are in the log2 domain (q pre-scaled by
-//            softmax_scale * log2 e); warp-shuffle max/sum; exp2 on MUFU.
-//       PV : lanes own output channels; V dequantized to fp16 like K;
-//            acc += p(fp16) * v(fp16) with the same mixed-precision FMA.
+//   warp 8 (producer): lane 0 posts each stage's transaction bytes, then the
+//     lanes issue the tile's 1-D bulk async copies together (cp.async.bulk,
+//     no tensor map, no multicast): K and V rows, q with a unit's first tile,
+//     per-token / per-group scales and zeros, into an NST-deep shared-memory
+//     ring. Each stage has a "full" (q, K) and a "fullv" (V) mbarrier with
+//     transaction bytes and an "empty" mbarrier the consumers arrive on.
+//   warps 0-7 (consumers, tensor pipe): each warp owns 16-position m-tiles
+//     of the tiles and keeps its own online-softmax state (m, l, acc) for the
+//     HB heads. Per m-tile:
+//       QK : mma.sync with K rows as A and the heads as the 8 columns of B.
+//            fp16: f16 m16n8k16 on q. INT8 / INT4: integer m16n8k32 on the
+//            raw codes (INT4 nibbles by masking) against q folded with the
+//            scales as byte limbs of 16 / 24-bit fixed point; the limbs are
+//            combined in fp32 (exact).
+//       softmax: log2 domain; the running maximum is raised only when a
+//            score exceeds it by more than kTau (one warp vote per tile).
+//       PV : f16 m16n8k16 with V^T as A and p^T (from the QK accumulator by
+//            movmatrix.trans) as B; INT8 / INT4 V codes enter as fp16
+//            subnormals with p * v_scale as the weight.
+//     INT4 folds the tile's K group scales into q first (one slice per warp,
+//     then a named barrier); with four heads per unit the consumers form two
+//     groups of four warps that take tiles in turn. Other INT4 group sizes
+//     (not multiples of 16) use a CUDA-core consumer that dequantizes to fp16
+//     exactly as the reference oracle does and multiplies with
+//     fma.rn.f32.f16.
 //   warp 9 (epilogue): at a unit boundary inside the CTA's range each
 //     consumer warp stores its raw (m, l, acc) in shared memory and arrives
 //     on a hand-off mbarrier, then goes on streaming; the epilogue warp merges
@@ -43,8 +50,9 @@
 //     segment is finished by all consumer warps together.
 //
 // The grid is launched with programmatic dependent launch: every thread runs
-// griddepcontrol.wait before the first global-memory access, so only the
-// launch and the prologue overlap the previous kernel on the stream.
+// griddepcontrol.wait before its first global-memory access, so only the
+// launch, the prologue and the producer's first address arithmetic overlap
+// the previous kernel on the stream.
 //
 // Every mbarrier wait is bounded (kMaxPolls); on expiry the kernel records
 // kDevWaitTimeout in the workspace error word, stops issuing copies, drains
@@ -1194,10 +1202,12 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
     }
 
     // ======================= consumer warps (tensor pipe) =================
-    // Per tile, each warp takes TW / 16 consecutive 16-position m-tiles and runs
-    // them side by side in one straight block: the QK MMAs of all of them, one
-    // softmax update (a single vote), then the PV MMAs of all of them, so the
-    // independent chains overlap and the tile loop carries little control flow.
+    // Each warp takes TW / 16 consecutive 16-position m-tiles at a time and
+    // runs them side by side in one straight block: the QK MMAs of all of them,
+    // one softmax update (a single vote), then the PV MMAs of all of them, so
+    // the independent chains overlap and the tile loop carries little control
+    // flow. (With warp groups, a warp covers NG such parts of its group's
+    // tiles.)
     if constexpr (MMA) {
         using M = MmaFmt<FMT>;
         const int w = warp;
