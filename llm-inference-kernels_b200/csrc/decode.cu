@@ -925,7 +925,6 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
     constexpr int TW = T / kNCW;  // positions per warp per tile
     constexpr int NP = TW / 4;    // QK passes (4 positions per pass)
     constexpr int PVC = F::PVC;
-    constexpr int SL = HB * kHeadDim + 2 * HB;  // partial slot stride (floats)
 
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x;
@@ -1374,13 +1373,13 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
             // copy of the tile body without the per-row masking.
             auto tile_body = [&](auto full_tag) {
                 constexpr bool FULL = decltype(full_tag)::value;
-                int d[MT][L][4];  // raw QK accumulators per m-tile and limb
-                float df[MT][4];  // fp16 KV: the QK accumulators
+                [[maybe_unused]] int d[MT][L][4];  // raw QK accumulators per m-tile and limb
+                [[maybe_unused]] float df[MT][4];  // fp16 KV: the QK accumulators
                 float zc[MT][2], dqc[MT][2];
                 if (FULL || nval > 0) {
                     // ---------------- QK (integer tensor pipe) ----------------
-                    int cur_gi = -1;
-    #pragma unroll
+                    [[maybe_unused]] int cur_gi = -1;
+#pragma unroll
                     for (int mi = 0; mi < MT; ++mi) {
                         if (FULL || 16 * mi < nval) {
                             if constexpr (F::KG) {
@@ -1390,7 +1389,7 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                                     cur_gi = gi;
                                     const uint4* bw = reinterpret_cast<const uint4*>(
                                         sb + p.off_w + ((gi * HB + (g < HB ? g : 0)) * 4 + r) * (L * 32));
-    #pragma unroll
+#pragma unroll
                                     for (int l = 0; l < L; ++l) {
                                         const uint4 u0 = bw[2 * l], u1 = bw[2 * l + 1];
                                         const bool on = g < HB;
@@ -1424,12 +1423,12 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                     {
                         // ---------------- scores ----------------
                         float sc[MT][4];
-    #pragma unroll
+#pragma unroll
                         for (int mi = 0; mi < MT; ++mi) {
-                            const int row = wt + 16 * mi + rg;
+                            [[maybe_unused]] const int row = wt + 16 * mi + rg;
                             const bool ok0 = FULL || 16 * mi + rg < nval, ok1 = FULL || 16 * mi + rg + 8 < nval;
                             float dv[4];
-    #pragma unroll
+#pragma unroll
                             for (int c = 0; c < 4; ++c) {
                                 if constexpr (FMT == kF16)
                                     dv[c] = df[mi][c];
@@ -1440,7 +1439,7 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                                                  static_cast<float>(d[mi][2][c]));
                             }
                             if constexpr (FMT == kF16) {
-    #pragma unroll
+#pragma unroll
                                 for (int c = 0; c < 4; ++c) sc[mi][c] = dv[c] * p.qscale;
                             } else if constexpr (FMT == kI8) {
                                 const __half* sks = reinterpret_cast<const __half*>(sb + p.off_ks);
@@ -1464,7 +1463,7 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                         // by more than kTau (weights up to 2^kTau, which keeps
                         // p * v_scale inside fp16 for every fp16 V): one vote.
                         float mx0 = -INFINITY, mx1 = -INFINITY;
-    #pragma unroll
+#pragma unroll
                         for (int mi = 0; mi < MT; ++mi) {
                             mx0 = fmaxf(mx0, fmaxf(sc[mi][0], sc[mi][2]));
                             mx1 = fmaxf(mx1, fmaxf(sc[mi][1], sc[mi][3]));
@@ -1483,7 +1482,7 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                             m_run[1] = mn1;
                             l_run[0] *= a0, zv[0] *= a0, lf[0] *= a0;
                             l_run[1] *= a1, zv[1] *= a1, lf[1] *= a1;
-    #pragma unroll
+#pragma unroll
                             for (int mt = 0; mt < 8; ++mt) {
                                 acc[mt][0] *= a0;
                                 acc[mt][1] *= a1;
@@ -1494,7 +1493,7 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                         const float mu0 = m_run[0] == -INFINITY ? 0.f : m_run[0];
                         const float mu1 = m_run[1] == -INFINITY ? 0.f : m_run[1];
                         uint32_t bf[MT][2];
-    #pragma unroll
+#pragma unroll
                         for (int mi = 0; mi < MT; ++mi) {
                             const int row = wt + 16 * mi + rg;
                             const bool ok0 = FULL || 16 * mi + rg < nval, ok1 = FULL || 16 * mi + rg + 8 < nval;
@@ -1526,7 +1525,7 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                             bf[mi][1] = movmatrix_trans(pr1);
                         }
                         // ---------------- PV (tensor pipe) ----------------
-    #pragma unroll
+#pragma unroll
                         for (int mi = 0; mi < MT; ++mi)
                             if (FULL || 16 * mi < nval)
                                 pv_kstep<FMT>(sb + p.off_v + (wt + 16 * mi + vr) * ROWB + M::VCB * g,
@@ -1859,7 +1858,7 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                             half2 c0[4], c1[4];
                             i4x8_to_h2<F::SIGNED>(kw.x, c0);
                             i4x8_to_h2<F::SIGNED>(kw.y, c1);
-    #pragma unroll
+#pragma unroll
                             for (int k = 0; k < 4; ++k) {
                                 if (F::ZK) {
                                     kk[k] = as_u32(__hfma2(c0[k], as_h2(kg[k]), as_h2(kgz[k])));
