@@ -1269,6 +1269,8 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
         const int phf = lane & 1;
         const int pcb = 32 * (lane >> 3) + 8 * ((lane >> 1) & 3);
         const int ph_head = SPLIT ? wg * HPW : w % HB;  // first of the warp's HPW heads
+        // INT4: the heads of the lane's two score columns (absent heads -> head 0)
+        [[maybe_unused]] const int zh0 = 2 * r < HB ? 2 * r : 0, zh1 = 2 * r + 1 < HB ? 2 * r + 1 : 0;
         float qh[HPW][4] = {};
         long long q_unit = -1;  // unit whose q is in qh
 
@@ -1369,6 +1371,7 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
             }
             int wt = wt0;  // first position of the half in progress
             int nval = 0;
+            [[maybe_unused]] int cur_gi = -1;  // INT4: K group whose weights are in Bq (this tile)
             // The common case, every position of the warp's share live, runs a
             // copy of the tile body without the per-row masking.
             auto tile_body = [&](auto full_tag) {
@@ -1378,7 +1381,6 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                 float zc[MT][2], dqc[MT][2];
                 if (FULL || nval > 0) {
                     // ---------------- QK (integer tensor pipe) ----------------
-                    [[maybe_unused]] int cur_gi = -1;
 #pragma unroll
                     for (int mi = 0; mi < MT; ++mi) {
                         if (FULL || 16 * mi < nval) {
@@ -1389,21 +1391,23 @@ __global__ void __launch_bounds__(threads_for<FMT, MMA>(), 1) decode_kernel(cons
                                     cur_gi = gi;
                                     const uint4* bw = reinterpret_cast<const uint4*>(
                                         sb + p.off_w + ((gi * HB + (g < HB ? g : 0)) * 4 + r) * (L * 32));
+                                    // columns of absent heads (g >= HB) repeat head 0,
+                                    // weights and constants alike; their results
+                                    // are never stored
 #pragma unroll
                                     for (int l = 0; l < L; ++l) {
                                         const uint4 u0 = bw[2 * l], u1 = bw[2 * l + 1];
-                                        const bool on = g < HB;
-                                        Bq[l][0][0] = on ? u0.x : 0u, Bq[l][0][1] = on ? u0.y : 0u;
-                                        Bq[l][1][0] = on ? u0.z : 0u, Bq[l][1][1] = on ? u0.w : 0u;
-                                        Bq[l][2][0] = on ? u1.x : 0u, Bq[l][2][1] = on ? u1.y : 0u;
-                                        Bq[l][3][0] = on ? u1.z : 0u, Bq[l][3][1] = on ? u1.w : 0u;
+                                        Bq[l][0][0] = u0.x, Bq[l][0][1] = u0.y;
+                                        Bq[l][1][0] = u0.z, Bq[l][1][1] = u0.w;
+                                        Bq[l][2][0] = u1.x, Bq[l][2][1] = u1.y;
+                                        Bq[l][3][0] = u1.z, Bq[l][3][1] = u1.w;
                                     }
                                     const float* zkp = reinterpret_cast<const float*>(sb + p.off_zk) + gi * HB;
                                     const float* dqp = zkp + p.ngw * HB;
-                                    zk[0] = 2 * r < HB ? zkp[2 * r] : 0.f;
-                                    zk[1] = 2 * r + 1 < HB ? zkp[2 * r + 1] : 0.f;
-                                    dk[0] = 2 * r < HB ? dqp[2 * r] : 0.f;
-                                    dk[1] = 2 * r + 1 < HB ? dqp[2 * r + 1] : 0.f;
+                                    zk[0] = zkp[zh0];
+                                    zk[1] = zkp[zh1];
+                                    dk[0] = dqp[zh0];
+                                    dk[1] = dqp[zh1];
                                 }
                               }
                             }
